@@ -1,0 +1,123 @@
+/*
+ * pentanet_b200.h -- C ABI of the B200 (sm_100a) PentaNet packed-weight path.
+ *
+ * Plain pointers and sizes only.  Every function returns an int status
+ * (PN_OK = 0).  All device pointers are caller-allocated; no entry point
+ * allocates memory.  Work is enqueued on the given CUDA stream (a cudaStream_t
+ * passed as void*, NULL = legacy default stream) and is asynchronous to the
+ * host unless stated otherwise.
+ *
+ * Packed weight format (penta_kernel.py:7-20, identical bytes): an (N, K_packs)
+ * row-major int32 array, K_packs = ceil(K/10); weight k = 10g+i of row n is the
+ * 3-bit code q+2 (q in {-2..2}) in bits [3i+2:3i] of word (n, g); bits 31:30
+ * are zero; K is padded with code 2.
+ */
+#ifndef PENTANET_B200_H
+#define PENTANET_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+enum pn_status_code {
+    PN_OK = 0,
+    PN_ERR_ARG = 1,         /* null pointer / invalid enum                     */
+    PN_ERR_SHAPE = 2,       /* dimension out of range or inconsistent          */
+    PN_ERR_ALIGN = 3,       /* pointer or row pitch not aligned as required    */
+    PN_ERR_DTYPE = 4,       /* unsupported element type                        */
+    PN_ERR_CUDA = 5,        /* a CUDA runtime/driver call failed               */
+    PN_ERR_UNSUPPORTED = 6, /* device is not sm_100                            */
+    PN_ERR_TIMEOUT = 7,     /* a kernel gave up on a bounded wait (device side)*/
+    PN_ERR_WORKSPACE = 8    /* workspace missing or too small                  */
+};
+
+/* ---- element types -------------------------------------------------------- */
+enum pn_dtype { PN_F32 = 0, PN_BF16 = 1, PN_I8 = 2, PN_I32 = 3 };
+
+/* ABI version of this header (bumped on any signature change). */
+int pn_abi_version(void);
+/* Static text for a status code. */
+const char *pn_status_string(int status);
+/* Message of the last failing call on this host thread ("" if none). */
+const char *pn_last_error(void);
+/* Device-side status word of the current device: a kernel that abandons a
+ * bounded wait records PN_ERR_TIMEOUT there.  Synchronises the device.  When
+ * reset != 0 the word is cleared after reading. */
+int pn_device_status(int reset, int *status_out);
+
+/* ---- packing: replaces quantize_and_pack (penta_kernel.py:42-78) ---------- */
+
+/* Bytes of workspace pn_absmean_scale needs. */
+size_t pn_absmean_workspace_size(void);
+
+/* gamma = max(mean|W|, 1e-8) as a float written to d_scale (device pointer):
+ * penta_kernel.py:57.  W has n_elems elements of w_dtype (PN_F32 or PN_BF16).
+ * The sum of |W| is accumulated in double in a fixed order, so the result is
+ * deterministic. */
+int pn_absmean_scale(const void *w, int w_dtype, int64_t n_elems, float *d_scale, void *workspace,
+                     size_t workspace_bytes, void *stream);
+
+/* Quantise with the device-resident scale and pack (penta_kernel.py:60-78):
+ * q = clamp(round_half_even(W / gamma), -2, 2) with IEEE float division,
+ * code = q + 2, ten codes per word, K padded with code 2.  W is (N, K)
+ * row-major, packed is (N, ceil(K/10)) int32. */
+int pn_quantize_pack(const void *w, int w_dtype, int64_t N, int64_t K, const float *d_scale,
+                     int32_t *packed, void *stream);
+
+/* ---- unpack: replaces unpack_weights (penta_kernel.py:81-90) and the C
+ *      penta_unpack_3bit (penta_avx2.c:41-59) ------------------------------- */
+
+/* out[n, k] = ((packed[n, k/10] >> 3*(k%10)) & 7) - 2 as int8, k < K_orig. */
+int pn_unpack(const int32_t *packed, int64_t N, int64_t K_packs, int64_t K_orig, int8_t *out, void *stream);
+
+/* ---- fused dequant-matmul: replaces penta_linear / _penta_matmul_kernel
+ *      (penta_kernel.py:111-278) ------------------------------------------- */
+
+/* Workspace bytes for pn_linear_bf16 / pn_linear_i8 at this shape (0 allowed
+ * when the result is 0).  kind: PN_BF16 or PN_I8. */
+size_t pn_linear_workspace_size(int kind, int64_t M, int64_t N, int64_t K);
+
+/* Y[M, N] = (X[M, K] . unpack(packed)^T) * scale (+ bias), fp32 accumulation.
+ * X: bf16 row-major (row pitch K elements).  packed: (N, K_packs) int32.
+ * bias: NULL or N bf16 values.  y_dtype PN_BF16 reproduces the reference's
+ * rounding (bf16(acc*scale), then bf16(. + bf16(bias)), penta_kernel.py:224,
+ * :275-276); PN_F32 returns the unrounded fp32 value acc*scale + bias.
+ * Workspace: pn_linear_workspace_size(PN_BF16, M, N, K) bytes, zero-filled once
+ * before its first use (the kernels leave it zeroed). */
+int pn_linear_bf16(const void *x, int64_t M, int64_t K, const int32_t *packed, int64_t N, int64_t K_packs,
+                   float scale, const void *bias, void *y, int y_dtype, void *workspace,
+                   size_t workspace_bytes, void *stream);
+
+/* ---- int8 activation path: replaces the int8 line of the reference
+ *      benchmark (penta_avx2_wrapper.py:130-131,137,147), per token --------- */
+
+/* Row pitch (bytes) of the quantised-activation buffer for a given K. */
+int64_t pn_act_i8_pitch(int64_t K);
+
+/* Per-token absmax int8 quantiser: s_x[m] = max|X[m,:]| / 127 (1 for an
+ * all-zero row), xq = clamp(round_half_even(X / s_x), -128, 127).  xq is
+ * (M, pitch) int8 with pitch = pn_act_i8_pitch(K); bytes k >= K are written
+ * as 0.  rowsum[m] = sum_k xq[m, k] (int32).  X is bf16 or fp32 (x_dtype). */
+int pn_quant_act_i8(const void *x, int x_dtype, int64_t M, int64_t K, int8_t *xq, int64_t xq_pitch, float *s_x,
+                    int32_t *rowsum, void *stream);
+
+/* acc[m, n] = sum_k xq[m, k] * w[n, k] (exact int32, = torch._int_mm(xq, w^T));
+ * Y = float(acc) * float(scale * s_x[m]) (+ bias).  acc_out: NULL or (M, N)
+ * int32 to receive the accumulators.  y: NULL or (M, N) of y_dtype
+ * (PN_BF16 / PN_F32).  xq/s_x/rowsum as produced by pn_quant_act_i8. */
+int pn_linear_i8(const int8_t *xq, int64_t xq_pitch, const float *s_x, const int32_t *rowsum, int64_t M,
+                 int64_t K, const int32_t *packed, int64_t N, int64_t K_packs, float scale, const void *bias,
+                 void *y, int y_dtype, int32_t *acc_out, void *workspace, size_t workspace_bytes,
+                 void *stream);
+
+/* Number of SMs of the current device (used to size launches and shards). */
+int pn_device_sm_count(int *count_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PENTANET_B200_H */

@@ -1,0 +1,519 @@
+// pn_dqmm.cu -- fused pentanary dequant-matmul on the sm_100a tensor cores.
+//
+// Computes Y[m, n] = scale * sum_k X[m, k] * w[n, k] for packed 3-bit weights
+// (the op of _penta_matmul_kernel, penta_kernel.py:111-224) as a swap-AB
+// tcgen05 GEMM: the weight tile is the MMA's A operand (128 weight rows = the
+// 128 TMEM lanes) and the activations are the B operand (BT tokens).
+//
+//   * Weights are streamed from HBM exactly once per (row tile, token tile):
+//     a loader warp stages 16 packed words (160 k) of each of the 128 rows per
+//     k-block into shared memory with cp.async; four unpack warps (one weight
+//     row per thread) turn their row's words into MMA operands in registers and
+//     write them straight into tensor memory with tcgen05.st -- the A operand
+//     never touches shared memory.
+//       kind::f16: exact bf16 weights c-2 (mantissa trick + one bf16x2 subtract)
+//       kind::i8 : the unsigned codes c in {0..4}; the -2 offset is applied in
+//                  the epilogue as -2 * rowsum(xq) (exact integer algebra).
+//   * Activations arrive by TMA (no multicast) in 32-byte swizzled slabs, one
+//     slab per MMA K-step.
+//   * One thread issues the MMAs; the fp32/int32 accumulator lives in TMEM and
+//     is read back by the unpack warps for the fused epilogue (scale, per-token
+//     activation scale, bias, bf16 rounding as the reference does it).
+//
+// Every barrier wait is bounded (pn_common.cuh); a CTA that gives up drains
+// its in-flight copies and MMAs, frees its tensor memory and exits, leaving
+// PN_ERR_TIMEOUT in the device status word.
+#include "pn_common.cuh"
+#include "pn_internal.h"
+
+#include <mutex>
+
+namespace pn {
+
+constexpr int kRows = 128;         // weight rows per tile (MMA M, TMEM lanes)
+constexpr int kWordsPerKB = 16;    // packed words per row per k-block (160 k)
+constexpr int kKB = kWordsPerKB * kPerWord;
+constexpr int kWPitch = 20;        // staged words per row (16 + 4 pad: conflict-free 128-bit reads)
+constexpr int kWStageBytes = kRows * kWPitch * 4;
+constexpr int kThreads = 192;      // warps 0-3 unpack+epilogue, 4 loader, 5 MMA
+constexpr int kTmemCols = 512;
+
+enum class Kind { F16, I8 };
+
+template <Kind KIND>
+struct KindT;
+template <>
+struct KindT<Kind::F16> {
+    static constexpr int kXElem = 2;       // bytes per activation element
+    static constexpr int kSlabElems = 16;  // elements per 32-byte slab = MMA K
+    static constexpr int kSteps = 10;      // MMAs per k-block
+    static constexpr int kACols = 80;      // TMEM columns of A per k-block (2 bf16 per column)
+};
+template <>
+struct KindT<Kind::I8> {
+    static constexpr int kXElem = 1;
+    static constexpr int kSlabElems = 32;
+    static constexpr int kSteps = 5;
+    static constexpr int kACols = 40;      // 4 codes per column
+};
+
+template <Kind KIND, int BT>
+struct Cfg {
+    using T = KindT<KIND>;
+    static constexpr int kSlabBytes = BT * 32;
+    static constexpr int kXStageBytes = kSlabBytes * T::kSteps;
+    static constexpr int kA0 = BT < 32 ? 32 : BT;                 // first A column (D occupies [0, BT))
+    static constexpr int kSA = (kTmemCols - kA0) / T::kACols > 6 ? 6 : (kTmemCols - kA0) / T::kACols;
+    static constexpr int kBudget = 200 * 1024;
+    // X ring gets what the W ring (8 stages for small tiles) leaves.
+    static constexpr int kSW = kXStageBytes >= 40 * 1024 ? 4 : (kXStageBytes >= 20 * 1024 ? 6 : 8);
+    static constexpr int kSXraw = (kBudget - kSW * kWStageBytes) / kXStageBytes;
+    static constexpr int kSX = kSXraw > 8 ? 8 : kSXraw;
+    static constexpr int kBarOff = kSX * kXStageBytes + kSW * kWStageBytes;
+    static constexpr int kNumBars = 2 * kSW + 2 * kSX + 2 * kSA + 3;
+    static constexpr int kSmem = kBarOff + kNumBars * 8 + 16 + 1024;  // + tmem slot/abort flag + align slack
+    static_assert(kSX >= 2, "activation ring too shallow");
+    static_assert(kSA >= 2, "TMEM operand ring too shallow");
+    static_assert(kA0 + kSA * T::kACols <= kTmemCols, "TMEM over-subscribed");
+    static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "token tile");
+};
+
+struct DqmmParams {
+    const int32_t* packed;
+    int64_t N, KP;
+    int M;
+    int n_row_tiles, n_items, n_kb;
+    float scale;
+    const __nv_bfloat16* bias;
+    void* y;
+    int y_f32;
+    int32_t* acc_out;
+    const float* s_x;
+    const int32_t* rowsum;
+};
+
+// bf16 weights of one packed word: five bf16x2 registers, natural k order
+// (register j holds k = 2j in the low half and k = 2j+1 in the high half).
+// (128 + c) is built in the mantissa of a bf16 with exponent 2^7, then 130 is
+// subtracted: exact c - 2 for every code.
+__device__ __forceinline__ uint32_t bf16_pair(uint32_t lo_src, uint32_t hi_src) {
+    uint32_t t = (lo_src & 0x00000007u) | (hi_src & 0x00070000u) | 0x43004300u;
+    uint32_t r;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(t), "r"(0x43024302u));
+    return r;
+}
+__device__ __forceinline__ void unpack_word_bf16(uint32_t p, uint32_t* r) {
+    r[0] = bf16_pair(p, p << 13);
+    r[1] = bf16_pair(p >> 6, p << 7);
+    r[2] = bf16_pair(p >> 12, p << 1);
+    r[3] = bf16_pair(p >> 18, p >> 5);
+    r[4] = bf16_pair(p >> 24, p >> 11);
+}
+
+// Unsigned codes of two packed words (20 weights) as five int8x4 registers in
+// natural k order.  Four codes at stride 3 are spread to stride 8 with two
+// carry-free multiplies (even and odd codes separately).
+__device__ __forceinline__ uint32_t spread4(uint32_t t) {
+    const uint32_t e = t & 0x1C7u;  // codes 0 and 2
+    const uint32_t o = t & 0xE38u;  // codes 1 and 3
+    return ((e * 0x401u) & 0x00070007u) | ((o * 0x8020u) & 0x07000700u);
+}
+__device__ __forceinline__ void unpack_pair_u8(uint32_t p0, uint32_t p1, uint32_t* r) {
+    const uint32_t lo = p0 | (p1 << 30);
+    const uint32_t hi = p1 >> 2;
+    r[0] = spread4(lo);
+    r[1] = spread4(lo >> 12);
+    r[2] = spread4(__funnelshift_r(lo, hi, 24));
+    r[3] = spread4(hi >> 4);
+    r[4] = spread4(hi >> 16);
+}
+
+__device__ __forceinline__ void cp_async_4_zfill(void* smem_dst, const void* gmem_src, bool valid) {
+    const uint32_t src_size = valid ? 4u : 0u;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src),
+                 "r"(src_size)
+                 : "memory");
+}
+
+// Bounded wait used while draining after an abort (ignores the abort flag).
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            record_status(PN_ERR_TIMEOUT);
+            return;
+        }
+    }
+}
+
+template <Kind KIND, int BT>
+__global__ void __launch_bounds__(kThreads, 1)
+    dqmm_kernel(const __grid_constant__ CUtensorMap xmap, const DqmmParams p) {
+    using C = Cfg<KIND, BT>;
+    using T = typename C::T;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem_x = smem;
+    uint32_t* smem_w = reinterpret_cast<uint32_t*>(smem + C::kSX * C::kXStageBytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+    uint64_t* full_w = bars;
+    uint64_t* empty_w = full_w + C::kSW;
+    uint64_t* full_x = empty_w + C::kSW;
+    uint64_t* empty_x = full_x + C::kSX;
+    uint64_t* full_a = empty_x + C::kSX;
+    uint64_t* empty_a = full_a + C::kSA;
+    uint64_t* acc_full = empty_a + C::kSA;
+    uint64_t* acc_empty = acc_full + 1;
+    uint64_t* drain = acc_empty + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kSW; ++s) {
+            mbar_init(&full_w[s], 32);
+            mbar_init(&empty_w[s], 4);
+        }
+        for (int s = 0; s < C::kSX; ++s) {
+            mbar_init(&full_x[s], 1);
+            mbar_init(&empty_x[s], 1);
+        }
+        for (int s = 0; s < C::kSA; ++s) {
+            mbar_init(&full_a[s], 4);
+            mbar_init(&empty_a[s], 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, 4);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 5) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    if (warp == 4 && lane == 0) tma_prefetch_desc(&xmap);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int n_kb = p.n_kb;
+
+    if (warp == 4) {
+        // ------------------------------------------------------- loader ----
+        uint32_t it = 0;
+        bool ok = true;
+        uint32_t issued_x = 0;
+        for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
+            const int64_t n0 = (int64_t)(item % p.n_row_tiles) * kRows;
+            const int m0 = (item / p.n_row_tiles) * BT;
+            for (int kb = 0; kb < n_kb; ++kb, ++it) {
+                const int sw = it % C::kSW;
+                if (!warp_wait(&empty_w[sw], ((it / C::kSW) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                uint32_t* dst = smem_w + sw * (kRows * kWPitch);
+                const int64_t g0 = (int64_t)kb * kWordsPerKB;
+#pragma unroll 4
+                for (int e = lane; e < kRows * kWordsPerKB; e += 32) {
+                    const int r = e >> 4;
+                    const int wd = e & 15;
+                    const int64_t n = n0 + r;
+                    const int64_t g = g0 + wd;
+                    const bool valid = (n < p.N) && (g < p.KP);
+                    const int32_t* src = valid ? (p.packed + n * p.KP + g) : p.packed;
+                    cp_async_4_zfill(dst + r * kWPitch + wd, src, valid);
+                }
+                cp_async_mbar_arrive_noinc(&full_w[sw]);
+
+                const int sx = it % C::kSX;
+                if (!warp_wait(&empty_x[sx], ((it / C::kSX) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full_x[sx], C::kXStageBytes);
+                    uint8_t* xs = smem_x + sx * C::kXStageBytes;
+#pragma unroll
+                    for (int j = 0; j < T::kSteps; ++j)
+                        tma_load_2d(xs + j * C::kSlabBytes, &xmap, &full_x[sx], (kb * T::kSteps + j) * T::kSlabElems,
+                                    m0);
+                }
+                ++issued_x;
+                __syncwarp();
+            }
+        }
+        cp_async_wait_all();
+        if (!ok && lane == 0) {
+            // Let every issued TMA land before the CTA can exit.
+            const uint32_t first = issued_x > (uint32_t)C::kSX ? issued_x - C::kSX : 0u;
+            for (uint32_t j = first; j < issued_x; ++j) mbar_wait_drain(&full_x[j % C::kSX], (j / C::kSX) & 1);
+        }
+    } else if (warp == 5) {
+        // ---------------------------------------------------------- MMA ----
+        if (lane == 0) {
+            uint32_t idesc;
+            if constexpr (KIND == Kind::F16)
+                idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BT >> 3) << 17) | ((128u >> 4) << 24);
+            else  // A = unsigned 8-bit codes, B = signed int8, D = s32
+                idesc = (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(BT >> 3) << 17) | ((128u >> 4) << 24);
+            uint32_t it = 0, n_local = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++n_local) {
+                if (!mbar_wait(acc_empty, (n_local & 1) ^ 1, abort_flag)) break;
+                tc_fence_after();
+                for (int kb = 0; kb < n_kb; ++kb, ++it) {
+                    const int sx = it % C::kSX;
+                    const int sa = it % C::kSA;
+                    if (!mbar_wait(&full_x[sx], (it / C::kSX) & 1, abort_flag)) { ok = false; break; }
+                    if (!mbar_wait(&full_a[sa], (it / C::kSA) & 1, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint8_t* xs = smem_x + sx * C::kXStageBytes;
+                    const uint32_t a_col = tmem_base + C::kA0 + sa * T::kACols;
+#pragma unroll
+                    for (int j = 0; j < T::kSteps; ++j) {
+                        const uint64_t bdesc = smem_desc_sw32(xs + j * C::kSlabBytes);
+                        const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
+                        if constexpr (KIND == Kind::F16)
+                            mma_f16_ts(tmem_base, a_col + j * 8, bdesc, idesc, acc);
+                        else
+                            mma_i8_ts(tmem_base, a_col + j * 8, bdesc, idesc, acc);
+                    }
+                    tc_commit(&empty_x[sx]);
+                    tc_commit(&empty_a[sa]);
+                }
+                if (!ok) break;
+                tc_commit(acc_full);
+            }
+            // Wait for every MMA this thread issued before tensor memory is freed.
+            tc_commit(drain);
+            mbar_wait_drain(drain, 0);
+        }
+        __syncwarp();
+    } else {
+        // ---------------------------------------------- unpack + epilogue ----
+        const int row = threadIdx.x;  // 0..127 = TMEM lane
+        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        uint32_t it = 0, n_local = 0;
+        bool ok = true;
+        for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++n_local) {
+            const int64_t n0 = (int64_t)(item % p.n_row_tiles) * kRows;
+            const int m0 = (item / p.n_row_tiles) * BT;
+            for (int kb = 0; kb < n_kb; ++kb, ++it) {
+                const int sw = it % C::kSW;
+                if (!warp_wait(&full_w[sw], (it / C::kSW) & 1, abort_flag)) { ok = false; break; }
+                const uint4* src = reinterpret_cast<const uint4*>(smem_w + sw * (kRows * kWPitch) + row * kWPitch);
+                uint32_t wv[16];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint4 v = src[q];
+                    wv[4 * q + 0] = v.x;
+                    wv[4 * q + 1] = v.y;
+                    wv[4 * q + 2] = v.z;
+                    wv[4 * q + 3] = v.w;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty_w[sw]);
+
+                const int sa = it % C::kSA;
+                if (!warp_wait(&empty_a[sa], ((it / C::kSA) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t a_addr = tmem_base + lane_base + C::kA0 + sa * T::kACols;
+                if constexpr (KIND == Kind::F16) {
+                    // 16 words -> 80 columns, stored 8 words (40 columns) at a time.
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        uint32_t cols[40];
+#pragma unroll
+                        for (int w = 0; w < 8; ++w) unpack_word_bf16(wv[8 * h + w], &cols[5 * w]);
+#pragma unroll
+                        for (int c = 0; c < 5; ++c) {
+                            uint32_t v8[8];
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) v8[i] = cols[8 * c + i];
+                            tmem_st8(a_addr + 40 * h + 8 * c, v8);
+                        }
+                    }
+                } else {
+                    uint32_t cols[40];
+#pragma unroll
+                    for (int w = 0; w < 8; ++w) unpack_pair_u8(wv[2 * w], wv[2 * w + 1], &cols[5 * w]);
+#pragma unroll
+                    for (int c = 0; c < 5; ++c) {
+                        uint32_t v8[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) v8[i] = cols[8 * c + i];
+                        tmem_st8(a_addr + 8 * c, v8);
+                    }
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full_a[sa]);
+            }
+            if (!ok) break;
+
+            // ------------------------------------------------- epilogue ----
+            if (!warp_wait(acc_full, n_local & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            const int64_t n = n0 + row;
+            float bias_f = 0.0f;
+            if (p.bias != nullptr && n < p.N) bias_f = __bfloat162float(p.bias[n]);
+#pragma unroll 1
+            for (int c0 = 0; c0 < BT; c0 += 16) {
+                if (m0 + c0 >= p.M) break;  // warp-uniform
+                uint32_t v[16];
+                tmem_ld16(tmem_base + lane_base + c0, v);
+                tmem_wait_ld();
+                if (n < p.N) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int m = m0 + c0 + j;
+                        if (m >= p.M) break;
+                        float yv;
+                        if constexpr (KIND == Kind::F16) {
+                            yv = __fmul_rn(__uint_as_float(v[j]), p.scale);
+                        } else {
+                            const int acc_i = (int)v[j] - 2 * __ldg(p.rowsum + m);
+                            if (p.acc_out) p.acc_out[(int64_t)m * p.N + n] = acc_i;
+                            const float f = __fmul_rn(p.scale, __ldg(p.s_x + m));
+                            yv = __fmul_rn((float)acc_i, f);
+                        }
+                        if (p.y != nullptr) {
+                            if (p.y_f32) {
+                                if (p.bias) yv = __fadd_rn(yv, bias_f);
+                                static_cast<float*>(p.y)[(int64_t)m * p.N + n] = yv;
+                            } else {
+                                __nv_bfloat16 t = __float2bfloat16_rn(yv);
+                                if (p.bias) t = __float2bfloat16_rn(__fadd_rn(__bfloat162float(t), bias_f));
+                                static_cast<__nv_bfloat16*>(p.y)[(int64_t)m * p.N + n] = t;
+                            }
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 5) tmem_dealloc(tmem_base, kTmemCols);
+}
+
+// ------------------------------------------------------------------ host ----
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    });
+    return fn;
+}
+
+int device_sm_count() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    return n;
+}
+
+size_t linear_workspace_bytes(int, int64_t, int64_t, int64_t) { return 0; }
+
+template <Kind KIND, int BT>
+static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, const char** why) {
+    using C = Cfg<KIND, BT>;
+    using T = typename C::T;
+    EncodeTiledFn encode = get_encode_fn();
+    if (!encode) {
+        *why = "cuTensorMapEncodeTiled unavailable";
+        return PN_ERR_CUDA;
+    }
+    // Activations (M, K) with row pitch x_pitch; one box = one 32-byte K-slab of
+    // BT rows, i.e. one MMA K-step.  Columns >= K and rows >= M are zero-filled.
+    CUtensorMap map;
+    const int64_t pitch_bytes = a.x_pitch * T::kXElem;
+    cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
+    cuuint64_t strides[1] = {(cuuint64_t)pitch_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)T::kSlabElems, (cuuint32_t)BT};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult cr = encode(&map, KIND == Kind::F16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
+                         2, const_cast<void*>(a.x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) {
+        *why = "cuTensorMapEncodeTiled rejected the activation layout";
+        return PN_ERR_ALIGN;
+    }
+    DqmmParams prm;
+    prm.packed = a.packed;
+    prm.N = a.N;
+    prm.KP = a.KP;
+    prm.M = (int)a.M;
+    prm.n_row_tiles = (int)((a.N + kRows - 1) / kRows);
+    const int n_tok_tiles = (int)((a.M + BT - 1) / BT);
+    prm.n_items = prm.n_row_tiles * n_tok_tiles;
+    // k-blocks covering the activation extent (slabs past it are zero-filled by TMA)
+    prm.n_kb = (int)((a.KP * kPerWord + kKB - 1) / kKB);
+    prm.scale = a.scale;
+    prm.bias = static_cast<const __nv_bfloat16*>(a.bias);
+    prm.y = a.y;
+    prm.y_f32 = a.y_dtype == PN_F32;
+    prm.acc_out = a.acc_out;
+    prm.s_x = a.s_x;
+    prm.rowsum = a.rowsum;
+
+    auto kern = dqmm_kernel<KIND, BT>;
+    static bool attr_done[64] = {};  // per instantiation and device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_done[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+        if (e != cudaSuccess) {
+            *err = e;
+            *why = "cudaFuncSetAttribute";
+            return PN_ERR_CUDA;
+        }
+        if (dev >= 0 && dev < 64) attr_done[dev] = true;
+    }
+    int sms = device_sm_count();
+    if (sms <= 0) sms = 148;
+    const int grid = prm.n_items < sms ? prm.n_items : sms;
+    kern<<<grid, kThreads, C::kSmem, s>>>(map, prm);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *err = e;
+        *why = "kernel launch";
+        return PN_ERR_CUDA;
+    }
+    return PN_OK;
+}
+
+template <Kind KIND>
+static int launch_kind(const LinearArgs& a, cudaStream_t s, cudaError_t* err, const char** why) {
+    if (a.M <= 16) return launch_bt<KIND, 16>(a, s, err, why);
+    if (a.M <= 32) return launch_bt<KIND, 32>(a, s, err, why);
+    if (a.M <= 64) return launch_bt<KIND, 64>(a, s, err, why);
+    if (a.M <= 128) return launch_bt<KIND, 128>(a, s, err, why);
+    return launch_bt<KIND, 256>(a, s, err, why);
+}
+
+int launch_linear(const LinearArgs& a, cudaStream_t s, cudaError_t* err, const char** why) {
+    *err = cudaSuccess;
+    *why = "";
+    if (a.M == 0 || a.N == 0) return PN_OK;
+    if (a.kind == PN_BF16) return launch_kind<Kind::F16>(a, s, err, why);
+    return launch_kind<Kind::I8>(a, s, err, why);
+}
+
+}  // namespace pn

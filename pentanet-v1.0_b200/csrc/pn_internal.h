@@ -1,0 +1,46 @@
+// pn_internal.h -- launchers shared between the kernel files and the C ABI.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace pn {
+
+size_t absmean_workspace_bytes();
+cudaError_t launch_absmean(const void* w, int dtype, int64_t n, float* d_scale, void* ws, cudaStream_t s);
+cudaError_t launch_quantize_pack(const void* w, int dtype, int64_t N, int64_t K, const float* d_scale,
+                                 int32_t* packed, cudaStream_t s);
+cudaError_t launch_unpack(const int32_t* packed, int64_t N, int64_t KP, int64_t K, int8_t* out, cudaStream_t s);
+
+int64_t act_i8_pitch(int64_t K);
+cudaError_t launch_quant_act_i8(const void* x, int x_dtype, int64_t M, int64_t K, int8_t* xq, int64_t pitch,
+                                float* s_x, int32_t* rowsum, cudaStream_t s);
+
+// Fused dequant-matmul on the tensor cores (tcgen05, A operand in TMEM).
+struct LinearArgs {
+    int kind;                 // PN_BF16 (kind::f16) or PN_I8 (kind::i8)
+    const void* x;            // bf16 X (M, K) or int8 Xq (M, pitch)
+    int64_t x_pitch;          // elements per X row
+    int64_t M, K, N, KP;
+    const int32_t* packed;
+    float scale;
+    const void* bias;         // bf16 (N) or null
+    void* y;                  // (M, N) or null (int8 path only)
+    int y_dtype;              // PN_BF16 / PN_F32
+    int32_t* acc_out;         // int8 path: (M, N) int32 or null
+    const float* s_x;         // int8 path
+    const int32_t* rowsum;    // int8 path
+    void* workspace;
+    size_t workspace_bytes;
+};
+size_t linear_workspace_bytes(int kind, int64_t M, int64_t N, int64_t K);
+// Returns a pn_status_code; CUDA errors are reported through *cuda_err.
+int launch_linear(const LinearArgs& a, cudaStream_t s, cudaError_t* cuda_err, const char** why);
+
+// CUDA-core path for shapes the tensor-core kernel does not take (bf16 X whose
+// row pitch is not a multiple of 16 elements).
+cudaError_t launch_linear_simt_bf16(const LinearArgs& a, cudaStream_t s);
+
+int device_sm_count();
+
+}  // namespace pn

@@ -1,0 +1,242 @@
+"""penta_kernel -- drop-in for the reference module of the same name
+(penta_kernel.py), backed by hand-written sm_100a kernels through a C ABI.
+
+Same public functions, argument meanings and error behaviour:
+
+    quantize_and_pack(weight)                         penta_kernel.py:42-78
+    unpack_weights(packed, K_orig)                    penta_kernel.py:81-90
+    memory_stats(N, K)                                penta_kernel.py:93-106
+    penta_linear(x, packed_w, scale, K_orig, bias)    penta_kernel.py:229-278
+
+plus the int8-activation path of the reference benchmark
+(penta_avx2_wrapper.py:130-131,137,147), per token:
+
+    quantize_activations_i8(x)
+    penta_linear_i8(x, packed_w, scale, K_orig, bias)
+
+Encoding (penta_kernel.py:7-20): weight q in {-2,-1,0,+1,+2} is stored as the
+3-bit code q+2; ten codes per int32 (bits [3i+2:3i] hold column 10g+i; bits
+31:30 are zero); K is padded to a multiple of 10 with code 2.  Packed tensors
+are byte-identical to the reference's.
+
+Unlike the reference module this one imports without Triton; it needs the
+built library and a CUDA device (no CPU fallback).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+try:
+    from . import penta_native as _nat
+except ImportError:  # flat import (this directory on sys.path, as a drop-in)
+    import penta_native as _nat
+
+# ── Constants (penta_kernel.py:35-37) ─────────────────────────────────────────
+_W_PER_INT32 = 10
+_BITS_PER_W = 3
+_PENTA_OFFSET = 2
+
+
+def _k_packs(K: int) -> int:
+    return (K + _W_PER_INT32 - 1) // _W_PER_INT32
+
+
+def _require_cuda(t: torch.Tensor, what: str) -> None:
+    assert t.is_cuda, f"{what} requires a CUDA tensor (sm_100a kernels; there is no CPU path)"
+
+
+# ── Packing / unpacking ───────────────────────────────────────────────────────
+
+def absmean_scale(weight: torch.Tensor) -> torch.Tensor:
+    """gamma = max(mean|W|, 1e-8) as a 0-dim float32 CUDA tensor (no host sync).
+    The sum of |W| runs in double in a fixed order (deterministic)."""
+    assert weight.dim() == 2
+    _require_cuda(weight, "absmean_scale")
+    w = weight.contiguous()
+    if w.dtype not in (torch.float32, torch.bfloat16):
+        w = w.float()
+    L = _nat.load()
+    ws = torch.empty(int(L.pn_absmean_workspace_size()), dtype=torch.uint8, device=w.device)
+    out = torch.empty((), dtype=torch.float32, device=w.device)
+    dt = _nat.PN_F32 if w.dtype == torch.float32 else _nat.PN_BF16
+    _nat.check(L.pn_absmean_scale(w.data_ptr(), dt, w.numel(), out.data_ptr(), ws.data_ptr(), ws.numel(),
+                                  _nat.stream_of(w)), "absmean_scale")
+    return out
+
+
+def quantize_and_pack(weight: torch.Tensor, scale: float | torch.Tensor | None = None
+                      ) -> tuple[torch.Tensor, int, float]:
+    """Quantize FP32/BF16 master weights to pentanary {-2..+2} and 3-bit pack.
+
+    Args:
+        weight : (N, K) FP32/BF16 CUDA tensor
+        scale  : optional absmean scale to use instead of computing it (a float
+                 or a 0-dim CUDA tensor); the reference always computes it.
+
+    Returns:
+        packed : (N, ceil(K/10)) int32, byte-identical to the reference
+        K_orig : K
+        scale  : python float (penta_kernel.py:57)
+    """
+    assert weight.dim() == 2
+    _require_cuda(weight, "quantize_and_pack")
+    N, K = weight.shape
+    w = weight.detach().contiguous()
+    if w.dtype not in (torch.float32, torch.bfloat16):
+        w = w.float()
+    if scale is None:
+        d_scale = absmean_scale(w)
+    elif isinstance(scale, torch.Tensor):
+        d_scale = scale.detach().to(device=w.device, dtype=torch.float32).reshape(())
+    else:
+        d_scale = torch.tensor(float(scale), dtype=torch.float32, device=w.device)
+    packed = torch.empty(N, _k_packs(K), dtype=torch.int32, device=w.device)
+    dt = _nat.PN_F32 if w.dtype == torch.float32 else _nat.PN_BF16
+    _nat.check(_nat.load().pn_quantize_pack(w.data_ptr(), dt, N, K, d_scale.data_ptr(), packed.data_ptr(),
+                                            _nat.stream_of(w)), "quantize_and_pack")
+    return packed, K, float(d_scale)
+
+
+def unpack_weights(packed: torch.Tensor, K_orig: int) -> torch.Tensor:
+    """Unpack 3-bit tensor -> int32 (N, K_orig) with values in {-2..+2}
+    (penta_kernel.py:81-90).  Use unpack_weights_i8 for the int8 form."""
+    return unpack_weights_i8(packed, K_orig).to(torch.int32)
+
+
+def unpack_weights_i8(packed: torch.Tensor, K_orig: int) -> torch.Tensor:
+    """Unpack to int8 (N, K_orig), the layout of penta_unpack_3bit (penta_avx2.c:41-59)."""
+    assert packed.dim() == 2 and packed.dtype == torch.int32
+    _require_cuda(packed, "unpack_weights")
+    N, K_packs = packed.shape
+    p = packed.contiguous()
+    out = torch.empty(N, K_orig, dtype=torch.int8, device=p.device)
+    _nat.check(_nat.load().pn_unpack(p.data_ptr(), N, K_packs, K_orig, out.data_ptr(), _nat.stream_of(p)),
+               "unpack_weights")
+    return out
+
+
+def memory_stats(N: int, K: int) -> dict:
+    """Memory footprint comparison for an (N, K) weight matrix (penta_kernel.py:93-106):
+    nominal 3 bits/weight, as the reference reports it."""
+    fp16_bytes = N * K * 2
+    packed_bytes = (N * K * _BITS_PER_W + 7) // 8
+    ternary_bytes = (N * K * 2 + 7) // 8
+    return {
+        "fp16_MB": fp16_bytes / 1e6,
+        "packed_MB": packed_bytes / 1e6,
+        "ternary_MB": ternary_bytes / 1e6,
+        "penta_vs_fp16_ratio": round(fp16_bytes / packed_bytes, 2),
+        "penta_vs_ternary_ratio": round(ternary_bytes / packed_bytes, 2),
+    }
+
+
+def storage_bytes(N: int, K: int) -> int:
+    """Actual bytes of the packed int32 tensor (4 * N * ceil(K/10))."""
+    return 4 * N * _k_packs(K)
+
+
+# ── Fused dequant-matmul ─────────────────────────────────────────────────────
+
+def penta_linear(x: torch.Tensor, packed_w: torch.Tensor, scale: float, K_orig: int,
+                 bias: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """Fast pentanary linear: Y = X @ W.T * scale + bias (penta_kernel.py:229-278).
+
+    Args:
+        x        : (..., K) bfloat16 activation on CUDA
+        packed_w : (N, K_packs) int32 packed weights on CUDA
+        scale    : scalar float (absmean scale from quantize_and_pack)
+        K_orig   : original K before padding
+        bias     : (N,) optional bias tensor
+        out_dtype: torch.bfloat16 (reference rounding) or torch.float32 (the
+                   unrounded fp32 result; not in the reference)
+
+    Returns:
+        y : (..., N) of out_dtype
+    """
+    assert x.is_cuda, "penta_linear requires CUDA"
+    assert x.dtype == torch.bfloat16, "Activations must be bfloat16"
+    assert packed_w.dtype == torch.int32
+    assert out_dtype in (torch.bfloat16, torch.float32)
+    orig_shape = x.shape
+    x_2d = x.contiguous().reshape(-1, orig_shape[-1])
+    M, K = x_2d.shape
+    N, K_packs = packed_w.shape
+    assert K == K_orig, f"Activation K={K} must match K_orig={K_orig}"
+    pw = packed_w.contiguous()
+    y = torch.empty(M, N, device=x.device, dtype=out_dtype)
+    b = None
+    if bias is not None:
+        b = bias.detach().to(device=x.device, dtype=torch.bfloat16).contiguous()
+        assert b.numel() == N
+    L = _nat.load()
+    ws_bytes = int(L.pn_linear_workspace_size(_nat.PN_BF16, M, N, K))
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
+    _nat.check(L.pn_linear_bf16(x_2d.data_ptr(), M, K, pw.data_ptr(), N, K_packs, ctypes.c_float(scale),
+                                _nat.ptr(b), y.data_ptr(),
+                                _nat.PN_F32 if out_dtype == torch.float32 else _nat.PN_BF16,
+                                _nat.ptr(ws), ws_bytes, _nat.stream_of(x_2d)), "penta_linear")
+    return y.reshape(*orig_shape[:-1], N)
+
+
+# ── int8 activation path ─────────────────────────────────────────────────────
+
+def quantize_activations_i8(x: torch.Tensor):
+    """Per-token absmax int8 quantiser (penta_avx2_wrapper.py:130-131 applied per row).
+
+    Returns (xq, s_x, rowsum): xq (M, pitch) int8 zero-padded past K (pitch =
+    ceil(K/32)*32; xq[:, :K] is the quantised activation), s_x (M,) float32,
+    rowsum (M,) int32 = xq.sum(1)."""
+    assert x.is_cuda and x.dtype in (torch.bfloat16, torch.float32)
+    x_2d = x.contiguous().reshape(-1, x.shape[-1])
+    M, K = x_2d.shape
+    L = _nat.load()
+    pitch = int(L.pn_act_i8_pitch(K))
+    xq = torch.empty(M, pitch, dtype=torch.int8, device=x.device)
+    s_x = torch.empty(M, dtype=torch.float32, device=x.device)
+    rowsum = torch.empty(M, dtype=torch.int32, device=x.device)
+    dt = _nat.PN_F32 if x_2d.dtype == torch.float32 else _nat.PN_BF16
+    _nat.check(L.pn_quant_act_i8(x_2d.data_ptr(), dt, M, K, xq.data_ptr(), pitch, s_x.data_ptr(),
+                                 rowsum.data_ptr(), _nat.stream_of(x_2d)), "quantize_activations_i8")
+    return xq, s_x, rowsum
+
+
+def penta_linear_i8_prequant(xq: torch.Tensor, s_x: torch.Tensor, rowsum: torch.Tensor, K_orig: int,
+                             packed_w: torch.Tensor, scale: float, bias: torch.Tensor | None = None,
+                             out_dtype: torch.dtype | None = torch.bfloat16, return_acc: bool = False):
+    """int8 x packed-weight GEMM on already-quantised activations.
+    acc = xq @ w.T exactly (int32, = torch._int_mm); y = float(acc) * float32(scale * s_x) (+ bias)."""
+    assert xq.is_cuda and xq.dtype == torch.int8 and xq.dim() == 2
+    assert packed_w.dtype == torch.int32
+    M, pitch = xq.shape
+    N, K_packs = packed_w.shape
+    assert K_packs == _k_packs(K_orig), "packed weights do not match K_orig"
+    pw = packed_w.contiguous()
+    y = torch.empty(M, N, device=xq.device, dtype=out_dtype) if out_dtype is not None else None
+    acc = torch.empty(M, N, device=xq.device, dtype=torch.int32) if return_acc else None
+    b = bias.detach().to(device=xq.device, dtype=torch.bfloat16).contiguous() if bias is not None else None
+    L = _nat.load()
+    ws_bytes = int(L.pn_linear_workspace_size(_nat.PN_I8, M, N, K_orig))
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=xq.device) if ws_bytes else None
+    ydt = _nat.PN_F32 if out_dtype == torch.float32 else _nat.PN_BF16
+    _nat.check(L.pn_linear_i8(xq.data_ptr(), pitch, s_x.data_ptr(), rowsum.data_ptr(), M, K_orig, pw.data_ptr(),
+                              N, K_packs, ctypes.c_float(scale), _nat.ptr(b), _nat.ptr(y), ydt, _nat.ptr(acc),
+                              _nat.ptr(ws), ws_bytes, _nat.stream_of(xq)), "penta_linear_i8")
+    return (y, acc) if return_acc else y
+
+
+def penta_linear_i8(x: torch.Tensor, packed_w: torch.Tensor, scale: float, K_orig: int,
+                    bias: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
+                    return_acc: bool = False):
+    """Prefill path: per-token int8 activations x packed weights on the int8
+    tensor cores, fused scale epilogue.  x: (..., K) bf16/fp32 CUDA."""
+    orig_shape = x.shape
+    assert orig_shape[-1] == K_orig, f"Activation K={orig_shape[-1]} must match K_orig={K_orig}"
+    xq, s_x, rowsum = quantize_activations_i8(x)
+    out = penta_linear_i8_prequant(xq, s_x, rowsum, K_orig, packed_w, scale, bias, out_dtype, return_acc)
+    N = packed_w.shape[0]
+    if return_acc:
+        y, acc = out
+        return y.reshape(*orig_shape[:-1], N), acc.reshape(*orig_shape[:-1], N)
+    return out.reshape(*orig_shape[:-1], N)

@@ -1,0 +1,90 @@
+"""Per-token int8 activation quantiser and the int8 tensor-core GEMM against the
+oracle: xq, s_x and int32 accumulators bit-exact (= torch._int_mm), outputs
+exact to the reference's epilogue formula (penta_avx2_wrapper.py:147)."""
+import numpy as np
+import pytest
+import torch
+
+from _util import assert_bf16_close, gen_act, gen_weight, golden
+from oracle import oracle as orc
+import penta_kernel as pk
+
+pytestmark = pytest.mark.gpu
+META, G = golden()
+
+
+@pytest.mark.parametrize("name", [n for n in META["cases"] if n.startswith("int8.")])
+def test_golden_int8_cases(cuda_device, name):
+    c = META["cases"][name]
+    x = gen_act(c["M"], c["K"], c["x_seed"]).to(cuda_device)
+    xq, s_x, rowsum = pk.quantize_activations_i8(x)
+    K = c["K"]
+    assert np.array_equal(xq[:, :K].cpu().numpy(), G[f"{name}.xq"])
+    assert not xq[:, K:].any()
+    assert np.array_equal(s_x.cpu().numpy(), G[f"{name}.sx"])
+    assert np.array_equal(rowsum.cpu().numpy(), G[f"{name}.xq"].astype(np.int64).sum(1))
+    packed = torch.from_numpy(G[f"{name}.packed"]).to(cuda_device)
+    y, acc = pk.penta_linear_i8_prequant(xq, s_x, rowsum, K, packed, c["scale"], out_dtype=torch.float32,
+                                         return_acc=True)
+    assert np.array_equal(acc.cpu().numpy(), G[f"{name}.acc"])
+    assert np.array_equal(y.cpu().numpy(), G[f"{name}.y"])
+
+
+@pytest.mark.parametrize("M,N,K", [
+    (1, 128, 160), (16, 130, 770), (33, 257, 1001), (64, 384, 4096), (200, 256, 320), (256, 128, 3072),
+    (257, 300, 1600), (512, 640, 4096),
+])
+def test_int8_gemm_exact(cuda_device, M, N, K):
+    w = gen_weight(N, K, seed=M * 3 + N + K)
+    packed, _, gamma = pk.quantize_and_pack(w.to(cuda_device))
+    x = gen_act(M, K, seed=M + 5 * K).to(torch.bfloat16)
+    y, acc = pk.penta_linear_i8(x.to(cuda_device), packed, gamma, K, out_dtype=torch.float32, return_acc=True)
+    xq, sx = orc.quant_act_i8(x.float().numpy())
+    w8 = orc.unpack(packed.cpu().numpy(), K)
+    want_acc = orc.matmul_i8(xq, w8)
+    assert np.array_equal(acc.cpu().numpy(), want_acc)
+    assert np.array_equal(y.cpu().numpy(), orc.dequant_i8(want_acc, sx, gamma))
+    yb = pk.penta_linear_i8(x.to(cuda_device), packed, gamma, K)
+    assert np.array_equal(yb.float().cpu().numpy(), orc.to_bf16_f32(orc.dequant_i8(want_acc, sx, gamma)))
+
+
+def test_int8_bias_and_zero_rows(cuda_device):
+    N, K = 200, 512
+    packed, _, gamma = pk.quantize_and_pack(gen_weight(N, K, seed=2).to(cuda_device))
+    x = gen_act(6, K, seed=3)
+    x[2] = 0
+    bias = torch.randn(N, generator=torch.Generator().manual_seed(1))
+    y = pk.penta_linear_i8(x.to(cuda_device), packed, gamma, K, bias.to(cuda_device), out_dtype=torch.float32)
+    xq, sx = orc.quant_act_i8(x.numpy())
+    assert sx[2] == 1.0
+    acc = orc.matmul_i8(xq, orc.unpack(packed.cpu().numpy(), K))
+    want = orc.dequant_i8(acc, sx, gamma) + bias.to(torch.bfloat16).float().numpy()[None, :]
+    assert np.array_equal(y.cpu().numpy(), want.astype(np.float32))
+    yb = pk.penta_linear_i8(x.to(cuda_device), packed, gamma, K, bias.to(cuda_device))
+    assert_bf16_close(yb.float().cpu().numpy(), want, what="int8 bias bf16")
+
+
+@pytest.mark.parametrize("K,N", [(4096, 4096), (4096, 11008), (11008, 4096)])
+def test_cfg3_full_size(cuda_device, K, N):
+    """7B-class prefill shapes at M=4096: exact int32 checksum of checksums
+    (sum_n acc[m, n] = xq[m] . colsum(w)) and exact oracle rows/columns."""
+    M = 4096
+    packed, _, gamma = pk.quantize_and_pack(gen_weight(N, K, seed=K * 7 + N).to(cuda_device))
+    x = gen_act(M, K, seed=N).to(torch.bfloat16).to(cuda_device)
+    xq, s_x, rowsum = pk.quantize_activations_i8(x)
+    y, acc = pk.penta_linear_i8_prequant(xq, s_x, rowsum, K, packed, gamma, out_dtype=torch.float32,
+                                         return_acc=True)
+    w8 = pk.unpack_weights_i8(packed, K)
+    # float64 sums of these integers are exact (all partial sums < 2^53)
+    xqd = xq[:, :K].double()
+    w8d = w8.double()
+    assert torch.equal(acc.double().sum(1), xqd @ w8d.sum(0))
+    assert torch.equal(acc.double().sum(0), xqd.sum(0) @ w8d.T)
+    rows = torch.tensor([0, 1, 2047, M - 1])
+    cols = torch.tensor([0, 5, N // 3, N - 1])
+    xq_np = xq[rows, :K].cpu().numpy()
+    want = orc.matmul_i8(xq_np, w8.cpu().numpy())
+    assert np.array_equal(acc[rows].cpu().numpy(), want)
+    want_c = orc.matmul_i8(xq[:, :K].cpu().numpy(), w8[cols].cpu().numpy())
+    assert np.array_equal(acc[:, cols].cpu().numpy(), want_c)
+    assert np.array_equal(y[rows].cpu().numpy(), orc.dequant_i8(want, s_x[rows].cpu().numpy(), gamma))

@@ -1,0 +1,147 @@
+"""penta_linear (bf16 activations, kind::f16 tensor-core path and the CUDA-core
+path for unaligned K) against the oracle and the reference's golden outputs.
+
+Tolerance (written here as the contract): fp32 outputs within rel 1e-3 / abs
+1e-3 of the oracle after scaling; bf16 outputs within one bf16 ulp (+ abs 1e-3)
+of the exact value, since bf16 rounding itself is coarser than rel 1e-3."""
+import numpy as np
+import pytest
+import torch
+
+from _util import assert_bf16_close, assert_close, gen_act, gen_weight, golden
+from oracle import oracle as orc
+import penta_kernel as pk
+
+pytestmark = pytest.mark.gpu
+META, G = golden()
+
+
+def _layer(N, K, seed, dev, std=0.02):
+    w = gen_weight(N, K, seed, std)
+    packed, _, gamma = pk.quantize_and_pack(w.to(dev))
+    w8 = orc.unpack(packed.cpu().numpy(), K)
+    return packed, gamma, w8
+
+
+def _check(x_bf16, packed, gamma, w8, K, bias=None, what=""):
+    """Run fp32-out and bf16-out through the C ABI and compare to the oracle."""
+    xf = x_bf16.float().cpu().numpy()
+    want = orc.matmul_f64(xf, w8, gamma)
+    if bias is not None:
+        want = want + bias.to(torch.bfloat16).float().cpu().numpy()[None, :]
+    y32 = pk.penta_linear(x_bf16, packed, gamma, K, bias, out_dtype=torch.float32)
+    assert y32.dtype == torch.float32
+    assert_close(y32.cpu().numpy(), want, what=what + " fp32")
+    y16 = pk.penta_linear(x_bf16, packed, gamma, K, bias)
+    assert y16.dtype == torch.bfloat16
+    assert_bf16_close(y16.float().cpu().numpy(), want, what=what + " bf16")
+    if bias is None:
+        # bf16 output = bf16(acc * scale) of the same accumulator (penta_kernel.py:224)
+        assert np.array_equal(y16.float().cpu().numpy(), orc.to_bf16_f32(y32.cpu().numpy()))
+    return y32
+
+
+@pytest.mark.parametrize("shape", [(768, 2304), (768, 768), (768, 3072), (3072, 768)])
+@pytest.mark.parametrize("M", [1, 4, 16])
+def test_cfg1_decode_sweep(cuda_device, shape, M):
+    K, N = shape
+    name = f"cfg1.{K}x{N}"
+    c = META["cases"][name]
+    packed, gamma, w8 = _layer(N, K, c["w_seed"], cuda_device)
+    x = gen_act(M, K, c[f"M{M}_x_seed"]).to(torch.bfloat16).to(cuda_device)
+    y32 = _check(x, packed, gamma, w8, K, what=f"{name} M={M}")
+    # the reference's own CPU kernel output (numba, penta_kernel_cpu.py)
+    assert_close(y32.cpu().numpy(), G[f"{name}.M{M}.y_numba"], what=f"{name} M={M} vs numba")
+
+
+def test_cfg0_shape(cuda_device):
+    c = META["cases"]["cfg0"]
+    packed, gamma, w8 = _layer(3072, 768, 0, cuda_device)
+    x = gen_act(8, 768, c["x_seed"])
+    xb = x.to(torch.bfloat16).to(cuda_device)
+    _check(xb, packed, gamma, w8, 768, what="cfg0")
+    # fp32 activations rounded to bf16 stay within the bar of the fp32 reference on this data
+    y = pk.penta_linear(xb, packed, gamma, 768, out_dtype=torch.float32).cpu().numpy()
+    assert np.abs(y - G["cfg0.y_numba"]).max() < 0.05
+
+
+@pytest.mark.parametrize("M,N,K", [
+    (1, 1, 16), (2, 130, 160), (3, 257, 1000), (17, 128, 320), (33, 200, 776), (64, 384, 1600),
+    (65, 128, 480), (100, 300, 2048), (129, 256, 640), (256, 130, 800), (300, 512, 3072), (1000, 260, 768),
+])
+def test_tensor_core_shapes(cuda_device, M, N, K):
+    packed, gamma, w8 = _layer(N, K, seed=M + N + K, dev=cuda_device, std=0.05)
+    x = gen_act(M, K, seed=7 * M + K).to(torch.bfloat16).to(cuda_device)
+    _check(x, packed, gamma, w8, K, what=f"M={M} N={N} K={K}")
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 5, 7), (3, 17, 13), (16, 40, 770), (5, 64, 1001), (40, 33, 10)])
+def test_unaligned_k_cuda_core_path(cuda_device, M, N, K):
+    packed, gamma, w8 = _layer(N, K, seed=N * K, dev=cuda_device, std=0.05)
+    x = gen_act(M, K, seed=M * K).to(torch.bfloat16).to(cuda_device)
+    _check(x, packed, gamma, w8, K, what=f"simt M={M} N={N} K={K}")
+
+
+def test_bias_and_batch_dims(cuda_device):
+    N, K = 300, 768
+    packed, gamma, w8 = _layer(N, K, seed=3, dev=cuda_device)
+    bias = torch.randn(N, generator=torch.Generator().manual_seed(9)).to(cuda_device)
+    x = gen_act(2 * 5, K, seed=4).to(torch.bfloat16).to(cuda_device).reshape(2, 5, K)
+    y = pk.penta_linear(x, packed, gamma, K, bias)
+    assert y.shape == (2, 5, N)
+    _check(x.reshape(10, K), packed, gamma, w8, K, bias=bias, what="bias")
+
+
+def test_small_golden_outputs(cuda_device):
+    for name in [n for n in META["cases"] if n.startswith("small.")]:
+        c = META["cases"][name]
+        packed = torch.from_numpy(G[f"{name}.packed"]).to(cuda_device)
+        x = gen_act(3, c["K"], c["x_seed"])
+        y = pk.penta_linear(x.to(torch.bfloat16).to(cuda_device), packed, c["scale"], c["K"],
+                            out_dtype=torch.float32).cpu().numpy()
+        w8 = orc.unpack(G[f"{name}.packed"], c["K"])
+        assert_close(y, orc.matmul_f64(x.to(torch.bfloat16).float().numpy(), w8, c["scale"]), what=name)
+
+
+def test_zero_and_empty(cuda_device):
+    packed, gamma, w8 = _layer(64, 160, seed=1, dev=cuda_device)
+    x = torch.zeros(5, 160, dtype=torch.bfloat16, device=cuda_device)
+    assert torch.count_nonzero(pk.penta_linear(x, packed, gamma, 160)) == 0
+    y = pk.penta_linear(torch.zeros(0, 160, dtype=torch.bfloat16, device=cuda_device), packed, gamma, 160)
+    assert y.shape == (0, 64)
+
+
+def test_errors_like_reference(cuda_device):
+    packed, gamma, _ = _layer(8, 40, seed=1, dev=cuda_device)
+    with pytest.raises(AssertionError, match="bfloat16"):
+        pk.penta_linear(torch.zeros(2, 40, device=cuda_device), packed, gamma, 40)
+    with pytest.raises(AssertionError, match="K_orig"):
+        pk.penta_linear(torch.zeros(2, 30, dtype=torch.bfloat16, device=cuda_device), packed, gamma, 40)
+
+
+def test_cfg4_full_size_properties(cuda_device):
+    """70B-class decode shapes at full size: linearity and a checksum-of-
+    checksums against the oracle (sum over n of y[m, n] = x[m] . colsum(w)),
+    plus exact oracle rows for a sample of outputs."""
+    for (K, N) in [(8192, 28672), (28672, 8192)]:
+        packed, gamma, _ = _layer(N, K, seed=K + N, dev=cuda_device)
+        M = 8
+        x = gen_act(M, K, seed=K).to(torch.bfloat16).to(cuda_device)
+        y = pk.penta_linear(x, packed, gamma, K, out_dtype=torch.float32).double()
+        # linearity: y(2x) = 2 y(x) exactly (power-of-two scaling)
+        y2 = pk.penta_linear(x * 2, packed, gamma, K, out_dtype=torch.float32).double()
+        assert torch.equal(y2, 2 * y)
+        # checksum of checksums via the unpacked column sums
+        w8 = pk.unpack_weights_i8(packed, K)
+        colsum = w8.to(torch.float64).sum(0)
+        want = (x.double() @ colsum) * gamma
+        got = y.sum(1)
+        assert torch.allclose(got, want, rtol=1e-6, atol=1e-3 * N ** 0.5)
+        rows = torch.tensor([0, 1, N // 2, N - 1])
+        sample = orc.matmul_f64(x.float().cpu().numpy(), w8[rows].cpu().numpy(), gamma)
+        assert_close(y[:, rows].cpu().numpy(), sample, what=f"cfg4 {K}->{N} sample")
+
+
+def test_no_device_timeouts(cuda_device):
+    import penta_native as nat
+    assert nat.device_status(reset=True) == 0
