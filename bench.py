@@ -1,0 +1,465 @@
+#!/usr/bin/env python
+"""Benchmark of the packed PentaLinear path on B200.
+
+Workload (headline): 70B-class decode GEMV -- the packed layers K->N =
+8192->28672 and 28672->8192 at batch M in {1, 8, 64} (bf16 activations,
+N(0,1); weights N(0,0.02) absmean-quantised and packed).  One step runs the
+six (shape, M) products once.  The metric is HBM GB/s of algorithmic bytes
+(4*N*ceil(K/10) packed weight bytes + 2*M*K activation bytes + 2*M*N output
+bytes per product) divided by device time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the reference's own CPU kernel (penta_avx2.c compiled
+from source into oracle/_ref/, or the oracle port when it is absent) on the
+same workload with all host threads, on a bounded row sample per step.
+
+At N > 1 (torchrun) every layer is sharded by output rows over the ranks and
+each product ends in an NCCL all-gather of the output shards (strong scaling:
+the total work is fixed).
+
+The printed JSON line carries the device-timed value, an end-to-end number
+through the public API with host buffers, the roofline of the dqmm kernel, a
+CPU baseline, kernel-launch counts and the SM clocks sampled during timing.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "pentanet-v1.0_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "PentaLinear GEMV HBM GB/s & GEMM int8 TOPS vs roofline; 124M fwd tokens/s"
+SHAPES = [(8192, 28672), (28672, 8192)]   # (K, N)
+BATCHES = [1, 8, 64]
+COPIES = 4                                  # weight copies per shape, rotated (4 x 2 x 94 MB >> L2)
+FALLBACK_HBM_GBS = 6650.0
+
+
+def k_packs(K: int) -> int:
+    return (K + 9) // 10
+
+
+def alg_bytes(M: int, K: int, N: int) -> int:
+    return 4 * N * k_packs(K) + 2 * M * K + 2 * M * N
+
+
+def launches_per_step():
+    return [(M, K, N) for M in BATCHES for (K, N) in SHAPES]
+
+
+def step_bytes(world: int = 1) -> int:
+    # algorithmic bytes of the whole (unsharded) layer products
+    return sum(alg_bytes(M, K, N) for (M, K, N) in launches_per_step())
+
+
+def measured_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d.get("bf16_tflops", 0)),
+                "source": "measured (MEASURED_PEAKS.json)"}
+    return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def profile_traffic():
+    """dram bytes per launch of the dqmm kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "dqmm_gemv_70b_decode.md")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith("traffic_bytes_per_launch_full_size:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+# --------------------------------------------------------------- clocks ----
+
+class ClockSampler:
+    """Samples SM clock, power and throttle reasons with NVML (every ~5 ms)
+    while the timed region runs."""
+
+    def __init__(self, device_indices):
+        self.samples = []
+        self.ok = False
+        self._stop = threading.Event()
+        self._th = None
+        self.max_mhz = None
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nv = nv
+            self.handles = [nv.nvmlDeviceGetHandleByIndex(i) for i in device_indices]
+            self.max_mhz = max(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM) for h in self.handles)
+            self.ok = True
+        except Exception:  # NVML unavailable: report no clocks rather than guess
+            self.ok = False
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            for h in self.handles:
+                try:
+                    sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((time.time(), sm, reasons))
+                except Exception:
+                    pass
+            time.sleep(0.005)
+
+    def start(self):
+        if self.ok:
+            self._th = threading.Thread(target=self._run, daemon=True)
+            self._th.start()
+
+    def stop(self):
+        if self._th:
+            self._stop.set()
+            self._th.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        nv = self.nv
+        names = {
+            "gpu_idle": getattr(nv, "nvmlClocksEventReasonGpuIdle", 0x1),
+            "sw_power_cap": getattr(nv, "nvmlClocksEventReasonSwPowerCap", 0x4),
+            "hw_slowdown": getattr(nv, "nvmlClocksEventReasonHwSlowdown", 0x8),
+            "sw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+            "hw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+            "hw_power_brake_slowdown": getattr(nv, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
+        }
+        seen = set()
+        for _, _, r in self.samples:
+            for k, bit in names.items():
+                if k != "gpu_idle" and r & bit:
+                    seen.add(k)
+        return {"sm_mhz": statistics.median(s for _, s, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(seen), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------- CPU reference -----
+
+def cpu_reference_rate(sample_rows: int, reps: int, warmup: int, seed: int = 0):
+    """The reference's CPU kernel (penta_matmul_avx2 over int8 weights from
+    penta_unpack_3bit, as penta_avx2_wrapper.py:37-94 runs it) on the six
+    products, restricted to the first `sample_rows` output rows of each layer.
+    Returns (GB/s of algorithmic bytes, seconds per sample, kind, cores, desc)."""
+    import numpy as np
+    import torch
+    from oracle import oracle as orc
+
+    kind = "reference" if orc.ref_avx2_available() else "port"
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    g = torch.Generator().manual_seed(seed)
+    layers = {}
+    for (K, N) in SHAPES:
+        n = min(sample_rows, N)
+        w = (torch.randn(n, K, generator=g) * 0.02).numpy()
+        packed, _, gamma = orc.quantize_pack(w)
+        w8 = orc.ref_avx2_unpack(packed, K) if kind == "reference" else orc.unpack(packed, K)
+        layers[(K, N)] = (w8, gamma, n)
+    xs = {(M, K): torch.randn(M, K, generator=g).to(torch.bfloat16).float().numpy()
+          for (M, K, _) in launches_per_step()}
+    outs = {(M, K, N): np.empty((M, layers[(K, N)][2]), dtype=np.float32) for (M, K, N) in launches_per_step()}
+
+    def one():
+        for (M, K, N) in launches_per_step():
+            w8, gamma, n = layers[(K, N)]
+            if kind == "reference":
+                orc.ref_avx2_linear(xs[(M, K)], w8, gamma, outs[(M, K, N)])
+            else:
+                outs[(M, K, N)][...] = orc.matmul_f32(xs[(M, K)], w8, gamma)
+
+    for _ in range(warmup):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        one()
+    dt = (time.perf_counter() - t0) / reps
+    sample_bytes = sum(alg_bytes(M, K, layers[(K, N)][2]) for (M, K, N) in launches_per_step())
+    desc = (f"rows 0..{sample_rows} of each layer (of 28672 / 8192), all six (shape, M) products per step; "
+            f"{'penta_matmul_avx2 (-O3 -mavx2 -mfma -fopenmp)' if kind == 'reference' else 'scalar oracle port'}")
+    return sample_bytes / dt / 1e9, dt, kind, cores, desc
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # the CPU reference runs once per node, on rank 0
+    rows = int(os.environ.get("PN_REF_ROWS", "2048"))
+    rate, dt, kind, cores, desc = cpu_reference_rate(rows, max(1, args.steps), args.warmup)
+    line = {"metric": METRIC, "value": round(rate, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "70B-class decode GEMV: K->N 8192->28672 and 28672->8192, M in {1,8,64}",
+                       "sample": desc},
+            "cpu_baseline": {"value": round(rate, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+                             "sample": desc},
+            "e2e": {"value": round(rate, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------ our arm -----
+
+def run_profile_case(args):
+    """Small case for ncu --set full: the 8192->28672 layer (94 MB packed, one
+    copy), one launch each at M = 1, 8, 64, after three warm-up launches."""
+    import torch
+    import penta_kernel as pk
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(1234)
+    K, N = SHAPES[0]
+    w = torch.randn(N, K, device=dev, generator=gen) * 0.02
+    packed, _, s = pk.quantize_and_pack(w)
+    del w
+    torch.cuda.empty_cache()
+    xs = {M: torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16) for M in BATCHES}
+    for _ in range(3):
+        pk.penta_linear(xs[1], packed, s, K)
+    for M in BATCHES:
+        pk.penta_linear(xs[M], packed, s, K)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": "dqmm 8192->28672", "launches": 3 + len(BATCHES)}))
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import penta_kernel as pk
+    import penta_dist as pd
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    # ---- weights: quantise + pack each full layer on the GPU, keep this rank's rows
+    gen = torch.Generator(device=dev).manual_seed(1234)
+    packed = {}
+    scales = {}
+    for (K, N) in SHAPES:
+        w = torch.randn(N, K, device=dev, generator=gen) * 0.02
+        p, _, s = pk.quantize_and_pack(w)
+        del w
+        lo, hi = pd.shard_range(N, rank, world)
+        base = p[lo:hi].contiguous()
+        del p
+        packed[(K, N)] = [base] + [base.clone() for _ in range(COPIES - 1)]
+        scales[(K, N)] = s
+    torch.cuda.synchronize()
+    xs = {(M, K): torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16) for (M, K, _) in launches_per_step()}
+
+    seq = launches_per_step()
+
+    def run_step(i: int, outs=None):
+        for l, (M, K, N) in enumerate(seq):
+            c = ((6 * i + l) // 2) % COPIES
+            y = pk.penta_linear(xs[(M, K)], packed[(K, N)][c], scales[(K, N)], K)
+            if world > 1:
+                y = pd.gather_columns(y, N, world)
+            if outs is not None:
+                outs.append(y)
+
+    for i in range(3):
+        run_step(i)
+    torch.cuda.synchronize()
+
+    # Graph capture (N = 1): one graph per step phase removes host launch cost.
+    graphs = []
+    if world == 1:
+        for ph in range(4):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                run_step(ph)
+            graphs.append(g)
+        torch.cuda.synchronize()
+
+    def step(i):
+        if graphs:
+            graphs[i % 4].replay()
+        else:
+            run_step(i)
+
+    for i in range(args.warmup):
+        step(i)
+    sampler = ClockSampler([local] if world == 1 else list(range(torch.cuda.device_count()))[:world]) \
+        if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+    stream = torch.cuda.current_stream()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    if sampler:
+        sampler.stop()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    ms_per_step = ms / args.steps
+    value = step_bytes() * args.steps / (ms * 1e-3) / 1e9
+
+    # ---- per-launch kernel durations (roofline): each (shape, M) alone, 20 launches, rotating copies
+    per = []
+    for (M, K, N) in seq:
+        n_loc = packed[(K, N)][0].shape[0]
+        reps = 20
+        if world == 1:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for r in range(reps):
+                    pk.penta_linear(xs[(M, K)], packed[(K, N)][r % COPIES], scales[(K, N)], K)
+            g.replay()
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            dur = e0.elapsed_time(e1) / reps
+            del g
+        else:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for r in range(reps):
+                pk.penta_linear(xs[(M, K)], packed[(K, N)][r % COPIES], scales[(K, N)], K)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            dur = e0.elapsed_time(e1) / reps
+        b = alg_bytes(M, K, n_loc)
+        per.append({"M": M, "K": K, "N": N, "rows_local": n_loc, "us": round(dur * 1e3, 2),
+                    "gbs": round(b / (dur * 1e-3) / 1e9, 1)})
+    peaks = measured_peaks()
+    tot_b = sum(alg_bytes(p["M"], p["K"], p["rows_local"]) for p in per)
+    tot_t = sum(p["us"] for p in per) * 1e-6
+    achieved = tot_b / tot_t / 1e9
+    traffic = profile_traffic()
+
+    # ---- end to end through the public API with host buffers (pinned), eager calls
+    xh = {k: v.cpu().pin_memory() for k, v in xs.items()}
+    yh = {(M, K, N): torch.empty(M, N, dtype=torch.bfloat16).pin_memory() for (M, K, N) in seq}
+    xd = {k: torch.empty_like(v) for k, v in xs.items()}
+
+    def e2e_step(i):
+        for l, (M, K, N) in enumerate(seq):
+            c = ((6 * i + l) // 2) % COPIES
+            xd[(M, K)].copy_(xh[(M, K)], non_blocking=True)
+            y = pk.penta_linear(xd[(M, K)], packed[(K, N)][c], scales[(K, N)], K)
+            if world > 1:
+                y = pd.gather_columns(y, N, world)
+            yh[(M, K, N)].copy_(y, non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 200))
+    for i in range(3):
+        e2e_step(i)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        tt = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+    e2e_val = step_bytes() * e2e_steps / (e2e_ms * 1e-3) / 1e9
+    h2d = sum(2 * M * K for (M, K, N) in seq)
+    d2h = sum(2 * M * N for (M, K, N) in seq)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        rate, dt, kind, cores, desc = cpu_reference_rate(int(os.environ.get("PN_REF_ROWS", "2048")), 2, 1)
+        cpu = {"value": round(rate, 3), "unit": "GB/s", "cores": cores, "kind": kind, "sample": desc}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "70B-class decode GEMV: K->N 8192->28672 and 28672->8192, M in {1,8,64}",
+                       "weights": "N(0,0.02) absmean-quantised, 3-bit packed (94 MB per matrix)",
+                       "activations": "bf16 N(0,1)",
+                       "l2": f"inputs larger than L2: {COPIES} weight copies per shape rotated "
+                             f"({COPIES * 2 * 94} MB); a buffer is reused after >= 7 other 94 MB launches",
+                       "parallelism": "single GPU" if world == 1 else f"output rows sharded x{world} + NCCL all-gather",
+                       "timing": "CUDA graphs of one step" if world == 1 else "eager launches"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                         "peak_source": peaks["source"], "kernel": "pn::dqmm_kernel<F16, BT>",
+                         "per_launch": per},
+            "e2e": {"value": round(e2e_val, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "path": "penta_kernel.penta_linear with pinned host x/y copies per call, eager"},
+            "cpu_baseline": cpu,
+            "gpu_launches": len(seq) * args.steps,
+            "clocks": sampler.summary() if sampler else None,
+        }
+        print(json.dumps(line), flush=True)
+
+    graphs.clear()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--profile", action="store_true", help="small fixed case for ncu captures")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.profile:
+        run_profile_case(args)
+    elif args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -58,10 +58,13 @@ def test_int8_bias_and_zero_rows(cuda_device):
     xq, sx = orc.quant_act_i8(x.numpy())
     assert sx[2] == 1.0
     acc = orc.matmul_i8(xq, orc.unpack(packed.cpu().numpy(), K))
-    want = orc.dequant_i8(acc, sx, gamma) + bias.to(torch.bfloat16).float().numpy()[None, :]
+    pre = orc.dequant_i8(acc, sx, gamma)
+    want = pre + bias.to(torch.bfloat16).float().numpy()[None, :]
     assert np.array_equal(y.cpu().numpy(), want.astype(np.float32))
     yb = pk.penta_linear_i8(x.to(cuda_device), packed, gamma, K, bias.to(cuda_device))
-    assert_bf16_close(yb.float().cpu().numpy(), want, what="int8 bias bf16")
+    # exactly the reference's double rounding of the exact epilogue value
+    assert np.array_equal(yb.float().cpu().numpy(), orc.bf16_linear_out(pre, bias.numpy()))
+    assert_bf16_close(yb.float().cpu().numpy(), want, what="int8 bias bf16", pre_bias=pre)
 
 
 @pytest.mark.parametrize("K,N", [(4096, 4096), (4096, 11008), (11008, 4096)])

@@ -26,15 +26,17 @@ def _layer(N, K, seed, dev, std=0.02):
 def _check(x_bf16, packed, gamma, w8, K, bias=None, what=""):
     """Run fp32-out and bf16-out through the C ABI and compare to the oracle."""
     xf = x_bf16.float().cpu().numpy()
-    want = orc.matmul_f64(xf, w8, gamma)
+    pre = orc.matmul_f64(xf, w8, gamma)
+    want = pre
     if bias is not None:
-        want = want + bias.to(torch.bfloat16).float().cpu().numpy()[None, :]
+        want = pre + bias.to(torch.bfloat16).float().cpu().numpy()[None, :]
     y32 = pk.penta_linear(x_bf16, packed, gamma, K, bias, out_dtype=torch.float32)
     assert y32.dtype == torch.float32
     assert_close(y32.cpu().numpy(), want, what=what + " fp32")
     y16 = pk.penta_linear(x_bf16, packed, gamma, K, bias)
     assert y16.dtype == torch.bfloat16
-    assert_bf16_close(y16.float().cpu().numpy(), want, what=what + " bf16")
+    assert_bf16_close(y16.float().cpu().numpy(), want, what=what + " bf16",
+                      pre_bias=None if bias is None else pre)
     if bias is None:
         # bf16 output = bf16(acc * scale) of the same accumulator (penta_kernel.py:224)
         assert np.array_equal(y16.float().cpu().numpy(), orc.to_bf16_f32(y32.cpu().numpy()))
