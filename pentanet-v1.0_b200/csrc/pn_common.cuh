@@ -65,22 +65,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Wall-clock limit of one barrier wait.  Healthy waits in these kernels last
+// Limit of one barrier wait, in SM clock cycles (2^32 cycles: 2.2 s at the
+// 1965 MHz boost clock, longer at lower clocks).  Healthy waits last
 // microseconds; a wait that reaches the limit means a producer is gone.
-constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
+constexpr long long kWaitLimitCycles = 1ll << 32;
+// Spins between two checks of the abort flag and the cycle counter (the
+// checks stay off the fast path of a wait that completes quickly).
+constexpr uint32_t kSpinsPerCheck = 64;
 
 // Bounded wait.  Returns false (and records PN_ERR_TIMEOUT) when the limit is
 // reached or another thread of the CTA has already aborted (*abort != 0).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
+    const long long t0 = clock64();
+    uint32_t spins = 0;
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (*abort) return false;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            *abort = 1;
-            record_status(PN_ERR_TIMEOUT);
-            return false;
+        if (++spins % kSpinsPerCheck == 0) {
+            if (*abort) return false;
+            if (clock64() - t0 > kWaitLimitCycles) {
+                *abort = 1;
+                record_status(PN_ERR_TIMEOUT);
+                return false;
+            }
         }
     }
 }

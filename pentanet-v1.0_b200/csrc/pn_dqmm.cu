@@ -35,7 +35,10 @@ constexpr int kWordsPerKB = 16;    // packed words per row per k-block (160 k)
 constexpr int kKB = kWordsPerKB * kPerWord;
 constexpr int kWPitch = 20;        // staged words per row (16 + 4 pad: conflict-free 128-bit reads)
 constexpr int kWStageBytes = kRows * kWPitch * 4;
-constexpr int kThreads = 192;      // warps 0-3 unpack+epilogue, 4 loader, 5 MMA
+constexpr int kUnpackWarps = 8;    // warps 0-7: unpack + epilogue (two per TMEM lane quarter)
+constexpr int kLoadWarp = 8;       // cp.async weight staging + activation TMA
+constexpr int kMmaWarp = 9;        // TMEM allocation + MMA issue
+constexpr int kThreads = 32 * (kUnpackWarps + 2);
 constexpr int kTmemCols = 512;
 
 enum class Kind { F16, I8 };
@@ -83,6 +86,7 @@ struct DqmmParams {
     int64_t N, KP;
     int M;
     int n_row_tiles, n_items, n_kb;
+    int vec16;  // packed rows 16-byte aligned: stage with 16-byte cp.async
     float scale;
     const __nv_bfloat16* bias;
     void* y;
@@ -128,6 +132,12 @@ __device__ __forceinline__ void unpack_pair_u8(uint32_t p0, uint32_t p1, uint32_
     r[4] = spread4(hi >> 16);
 }
 
+__device__ __forceinline__ void cp_async_16_zfill(void* smem_dst, const void* gmem_src, bool valid) {
+    const uint32_t src_size = valid ? 16u : 0u;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src),
+                 "r"(src_size)
+                 : "memory");
+}
 __device__ __forceinline__ void cp_async_4_zfill(void* smem_dst, const void* gmem_src, bool valid) {
     const uint32_t src_size = valid ? 4u : 0u;
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src),
@@ -137,9 +147,9 @@ __device__ __forceinline__ void cp_async_4_zfill(void* smem_dst, const void* gme
 
 // Bounded wait used while draining after an abort (ignores the abort flag).
 __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
-    const uint64_t t0 = globaltimer_ns();
+    const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (clock64() - t0 > kWaitLimitCycles) {
             record_status(PN_ERR_TIMEOUT);
             return;
         }
@@ -174,27 +184,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kSW; ++s) {
             mbar_init(&full_w[s], 32);
-            mbar_init(&empty_w[s], 4);
+            mbar_init(&empty_w[s], kUnpackWarps);
         }
         for (int s = 0; s < C::kSX; ++s) {
             mbar_init(&full_x[s], 1);
             mbar_init(&empty_x[s], 1);
         }
         for (int s = 0; s < C::kSA; ++s) {
-            mbar_init(&full_a[s], 4);
+            mbar_init(&full_a[s], kUnpackWarps);
             mbar_init(&empty_a[s], 1);
         }
         mbar_init(acc_full, 1);
-        mbar_init(acc_empty, 4);
+        mbar_init(acc_empty, kUnpackWarps);
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
-    if (warp == 5) {
+    if (warp == kMmaWarp) {
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
-    if (warp == 4 && lane == 0) tma_prefetch_desc(&xmap);
+    if (warp == kLoadWarp && lane == 0) tma_prefetch_desc(&xmap);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -202,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int n_kb = p.n_kb;
 
-    if (warp == 4) {
+    if (warp == kLoadWarp) {
         // ------------------------------------------------------- loader ----
         uint32_t it = 0;
         bool ok = true;
@@ -210,20 +220,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
             const int64_t n0 = (int64_t)(item % p.n_row_tiles) * kRows;
             const int m0 = (item / p.n_row_tiles) * BT;
+            const int64_t rows_left = p.N - n0;
             for (int kb = 0; kb < n_kb; ++kb, ++it) {
                 const int sw = it % C::kSW;
                 if (!warp_wait(&empty_w[sw], ((it / C::kSW) & 1) ^ 1, abort_flag)) { ok = false; break; }
                 uint32_t* dst = smem_w + sw * (kRows * kWPitch);
                 const int64_t g0 = (int64_t)kb * kWordsPerKB;
+                if (p.vec16) {
+                    // 128 rows x 4 chunks of 16 bytes; K_packs % 4 == 0 keeps chunks whole and aligned
+                    const int q = lane & 3;
+                    const bool gvalid = g0 + 4 * q < p.KP;
+                    const int32_t* src = p.packed + (n0 + (lane >> 2)) * p.KP + g0 + 4 * q;
 #pragma unroll 4
-                for (int e = lane; e < kRows * kWordsPerKB; e += 32) {
-                    const int r = e >> 4;
-                    const int wd = e & 15;
-                    const int64_t n = n0 + r;
-                    const int64_t g = g0 + wd;
-                    const bool valid = (n < p.N) && (g < p.KP);
-                    const int32_t* src = valid ? (p.packed + n * p.KP + g) : p.packed;
-                    cp_async_4_zfill(dst + r * kWPitch + wd, src, valid);
+                    for (int j = 0; j < kRows / 8; ++j) {
+                        const int r = (lane >> 2) + 8 * j;
+                        const bool valid = gvalid && r < rows_left;
+                        cp_async_16_zfill(dst + r * kWPitch + 4 * q, valid ? src + (int64_t)8 * j * p.KP : p.packed,
+                                          valid);
+                    }
+                } else {
+                    const int wd = lane & 15;
+                    const bool gvalid = g0 + wd < p.KP;
+                    const int32_t* src = p.packed + (n0 + (lane >> 4)) * p.KP + g0 + wd;
+#pragma unroll 8
+                    for (int j = 0; j < kRows / 2; ++j) {
+                        const int r = (lane >> 4) + 2 * j;
+                        const bool valid = gvalid && r < rows_left;
+                        cp_async_4_zfill(dst + r * kWPitch + wd, valid ? src + (int64_t)2 * j * p.KP : p.packed,
+                                         valid);
+                    }
                 }
                 cp_async_mbar_arrive_noinc(&full_w[sw]);
 
@@ -247,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t first = issued_x > (uint32_t)C::kSX ? issued_x - C::kSX : 0u;
             for (uint32_t j = first; j < issued_x; ++j) mbar_wait_drain(&full_x[j % C::kSX], (j / C::kSX) & 1);
         }
-    } else if (warp == 5) {
+    } else if (warp == kMmaWarp) {
         // ---------------------------------------------------------- MMA ----
         if (lane == 0) {
             uint32_t idesc;
@@ -290,8 +315,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else {
         // ---------------------------------------------- unpack + epilogue ----
-        const int row = threadIdx.x;  // 0..127 = TMEM lane
-        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        // Warps q and q+4 share TMEM lane quarter q (rows 32q..32q+31); warp
+        // half h takes words [8h, 8h+8) of every 16-word k-block.
+        const int quarter = warp & 3;
+        const int half = warp >> 2;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         uint32_t it = 0, n_local = 0;
         bool ok = true;
         for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++n_local) {
@@ -300,10 +329,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kb = 0; kb < n_kb; ++kb, ++it) {
                 const int sw = it % C::kSW;
                 if (!warp_wait(&full_w[sw], (it / C::kSW) & 1, abort_flag)) { ok = false; break; }
-                const uint4* src = reinterpret_cast<const uint4*>(smem_w + sw * (kRows * kWPitch) + row * kWPitch);
-                uint32_t wv[16];
+                const uint4* src =
+                    reinterpret_cast<const uint4*>(smem_w + sw * (kRows * kWPitch) + row * kWPitch + 8 * half);
+                uint32_t wv[8];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
+                for (int q = 0; q < 2; ++q) {
                     const uint4 v = src[q];
                     wv[4 * q + 0] = v.x;
                     wv[4 * q + 1] = v.y;
@@ -316,26 +346,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int sa = it % C::kSA;
                 if (!warp_wait(&empty_a[sa], ((it / C::kSA) & 1) ^ 1, abort_flag)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t a_addr = tmem_base + lane_base + C::kA0 + sa * T::kACols;
+                const uint32_t a_addr = tmem_base + lane_base + C::kA0 + sa * T::kACols + half * (T::kACols / 2);
                 if constexpr (KIND == Kind::F16) {
-                    // 16 words -> 80 columns, stored 8 words (40 columns) at a time.
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        uint32_t cols[40];
-#pragma unroll
-                        for (int w = 0; w < 8; ++w) unpack_word_bf16(wv[8 * h + w], &cols[5 * w]);
-#pragma unroll
-                        for (int c = 0; c < 5; ++c) {
-                            uint32_t v8[8];
-#pragma unroll
-                            for (int i = 0; i < 8; ++i) v8[i] = cols[8 * c + i];
-                            tmem_st8(a_addr + 40 * h + 8 * c, v8);
-                        }
-                    }
-                } else {
+                    // 8 words -> 40 columns
                     uint32_t cols[40];
 #pragma unroll
-                    for (int w = 0; w < 8; ++w) unpack_pair_u8(wv[2 * w], wv[2 * w + 1], &cols[5 * w]);
+                    for (int w = 0; w < 8; ++w) unpack_word_bf16(wv[w], &cols[5 * w]);
 #pragma unroll
                     for (int c = 0; c < 5; ++c) {
                         uint32_t v8[8];
@@ -343,6 +359,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int i = 0; i < 8; ++i) v8[i] = cols[8 * c + i];
                         tmem_st8(a_addr + 8 * c, v8);
                     }
+                } else {
+                    // 8 words -> 4 pairs -> 20 columns
+                    uint32_t cols[20];
+#pragma unroll
+                    for (int w = 0; w < 4; ++w) unpack_pair_u8(wv[2 * w], wv[2 * w + 1], &cols[5 * w]);
+#pragma unroll
+                    for (int c = 0; c < 2; ++c) {
+                        uint32_t v8[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) v8[i] = cols[8 * c + i];
+                        tmem_st8(a_addr + 8 * c, v8);
+                    }
+                    uint32_t v4[4] = {cols[16], cols[17], cols[18], cols[19]};
+                    tmem_st4(a_addr + 16, v4);
                 }
                 tmem_wait_st();
                 tc_fence_before();
@@ -358,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float bias_f = 0.0f;
             if (p.bias != nullptr && n < p.N) bias_f = __bfloat162float(p.bias[n]);
 #pragma unroll 1
-            for (int c0 = 0; c0 < BT; c0 += 16) {
+            for (int c0 = 16 * half; c0 < BT; c0 += 32) {
                 if (m0 + c0 >= p.M) break;  // warp-uniform
                 uint32_t v[16];
                 tmem_ld16(tmem_base + lane_base + c0, v);
@@ -399,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 5) tmem_dealloc(tmem_base, kTmemCols);
+    if (warp == kMmaWarp) tmem_dealloc(tmem_base, kTmemCols);
 }
 
 // ------------------------------------------------------------------ host ----
@@ -465,6 +495,7 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     prm.n_items = prm.n_row_tiles * n_tok_tiles;
     // k-blocks covering the activation extent (slabs past it are zero-filled by TMA)
     prm.n_kb = (int)((a.KP * kPerWord + kKB - 1) / kKB);
+    prm.vec16 = (a.KP % 4 == 0) && (reinterpret_cast<uintptr_t>(a.packed) % 16 == 0);
     prm.scale = a.scale;
     prm.bias = static_cast<const __nv_bfloat16*>(a.bias);
     prm.y = a.y;
