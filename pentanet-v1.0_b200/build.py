@@ -42,7 +42,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if not force and up_to_date():
         return OUT
     tmp = OUT + ".tmp"
-    cmd = [nvcc(), *NVCC_FLAGS, "-o", tmp, *[os.path.join(HERE, s) for s in SOURCES]]
+    cmd = [nvcc(), *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"), "-o", tmp,
+           *[os.path.join(HERE, s) for s in SOURCES]]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), flush=True)

@@ -9,7 +9,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
-#include "../../include/pentanet_b200.h"
+#include "pentanet_b200.h"
 
 namespace pn {
 

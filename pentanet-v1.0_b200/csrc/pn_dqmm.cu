@@ -36,9 +36,10 @@ constexpr int kKB = kWordsPerKB * kPerWord;
 constexpr int kWPitch = 20;        // staged words per row (16 + 4 pad: conflict-free 128-bit reads)
 constexpr int kWStageBytes = kRows * kWPitch * 4;
 constexpr int kUnpackWarps = 8;    // warps 0-7: unpack + epilogue (two per TMEM lane quarter)
-constexpr int kLoadWarp = 8;       // cp.async weight staging + activation TMA
-constexpr int kMmaWarp = 9;        // TMEM allocation + MMA issue
-constexpr int kThreads = 32 * (kUnpackWarps + 2);
+constexpr int kLoadWarp = 8;       // cp.async weight/activation staging (+ activation TMA for large tiles)
+constexpr int kMmaWarp = 9;        // TMEM allocation + MMA issue; warps 9.. issue MMAs
+constexpr int kMaxIssuers = 4;
+constexpr int kThreads = 32 * (kUnpackWarps + 1 + kMaxIssuers);
 constexpr int kTmemCols = 512;
 
 enum class Kind { F16, I8 };
@@ -63,9 +64,18 @@ struct KindT<Kind::I8> {
 template <Kind KIND, int BT>
 struct Cfg {
     using T = KindT<KIND>;
+    // Small token tiles (decode): activations are staged with cp.async (only the
+    // real token rows, 16 bytes per copy) and several warps issue MMAs, each
+    // into its own accumulator -- one thread can issue an MMA only every ~50
+    // cycles, which small-N MMAs cannot hide.  Large tiles (prefill): TMA boxes
+    // and one issuer.
+    static constexpr bool kXTma = BT >= 128;
+    static constexpr int kIssuers = BT <= 32 ? 4 : (BT <= 64 ? 2 : 1);
     static constexpr int kSlabBytes = BT * 32;
     static constexpr int kXStageBytes = kSlabBytes * T::kSteps;
-    static constexpr int kA0 = BT < 32 ? 32 : BT;                 // first A column (D occupies [0, BT))
+    static constexpr int kChunksPerRow = kKB * T::kXElem / 16;      // 16-byte pieces of one row per k-block
+    static constexpr int kDCols = kIssuers * BT;                  // accumulators D_0..D_{kIssuers-1}
+    static constexpr int kA0 = kDCols < 32 ? 32 : kDCols;         // first A column
     static constexpr int kSA = (kTmemCols - kA0) / T::kACols > 6 ? 6 : (kTmemCols - kA0) / T::kACols;
     static constexpr int kBudget = 200 * 1024;
     // X ring gets what the W ring (8 stages for small tiles) leaves.
@@ -73,7 +83,7 @@ struct Cfg {
     static constexpr int kSXraw = (kBudget - kSW * kWStageBytes) / kXStageBytes;
     static constexpr int kSX = kSXraw > 8 ? 8 : kSXraw;
     static constexpr int kBarOff = kSX * kXStageBytes + kSW * kWStageBytes;
-    static constexpr int kNumBars = 2 * kSW + 2 * kSX + 2 * kSA + 3;
+    static constexpr int kNumBars = 2 * kSW + 2 * kSX + 2 * kSA + 3 + kIssuers;
     static constexpr int kSmem = kBarOff + kNumBars * 8 + 16 + 1024;  // + tmem slot/abort flag + align slack
     static_assert(kSX >= 2, "activation ring too shallow");
     static_assert(kSA >= 2, "TMEM operand ring too shallow");
@@ -87,6 +97,8 @@ struct DqmmParams {
     int M;
     int n_row_tiles, n_items, n_kb;
     int vec16;  // packed rows 16-byte aligned: stage with 16-byte cp.async
+    const uint8_t* x;     // activations (cp.async path): bf16 or int8 rows of x_pitch_bytes
+    int64_t x_pitch_bytes;
     float scale;
     const __nv_bfloat16* bias;
     void* y;
@@ -174,8 +186,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* empty_a = full_a + C::kSA;
     uint64_t* acc_full = empty_a + C::kSA;
     uint64_t* acc_empty = acc_full + 1;
-    uint64_t* drain = acc_empty + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* drain = acc_empty + 1;  // one per issuer
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + C::kIssuers);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -187,16 +199,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&empty_w[s], kUnpackWarps);
         }
         for (int s = 0; s < C::kSX; ++s) {
-            mbar_init(&full_x[s], 1);
+            mbar_init(&full_x[s], C::kXTma ? 1 : 32);
             mbar_init(&empty_x[s], 1);
         }
         for (int s = 0; s < C::kSA; ++s) {
             mbar_init(&full_a[s], kUnpackWarps);
             mbar_init(&empty_a[s], 1);
         }
-        mbar_init(acc_full, 1);
+        mbar_init(acc_full, C::kIssuers);
         mbar_init(acc_empty, kUnpackWarps);
-        mbar_init(drain, 1);
+        for (int i = 0; i < C::kIssuers; ++i) mbar_init(&drain[i], 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -204,7 +216,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
-    if (warp == kLoadWarp && lane == 0) tma_prefetch_desc(&xmap);
+    if constexpr (C::kXTma) {
+        if (warp == kLoadWarp && lane == 0) tma_prefetch_desc(&xmap);
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -221,6 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int64_t n0 = (int64_t)(item % p.n_row_tiles) * kRows;
             const int m0 = (item / p.n_row_tiles) * BT;
             const int64_t rows_left = p.N - n0;
+            const int tok_rows = p.M - m0 < BT ? p.M - m0 : BT;  // real token rows of this tile
             for (int kb = 0; kb < n_kb; ++kb, ++it) {
                 const int sw = it % C::kSW;
                 if (!warp_wait(&empty_w[sw], ((it / C::kSW) & 1) ^ 1, abort_flag)) { ok = false; break; }
@@ -254,38 +269,64 @@ __global__ void __launch_bounds__(kThreads, 1)
 
                 const int sx = it % C::kSX;
                 if (!warp_wait(&empty_x[sx], ((it / C::kSX) & 1) ^ 1, abort_flag)) { ok = false; break; }
-                if (lane == 0) {
-                    mbar_arrive_expect_tx(&full_x[sx], C::kXStageBytes);
-                    uint8_t* xs = smem_x + sx * C::kXStageBytes;
+                uint8_t* xs = smem_x + sx * C::kXStageBytes;
+                if constexpr (C::kXTma) {
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(&full_x[sx], C::kXStageBytes);
 #pragma unroll
-                    for (int j = 0; j < T::kSteps; ++j)
-                        tma_load_2d(xs + j * C::kSlabBytes, &xmap, &full_x[sx], (kb * T::kSteps + j) * T::kSlabElems,
-                                    m0);
+                        for (int j = 0; j < T::kSteps; ++j)
+                            tma_load_2d(xs + j * C::kSlabBytes, &xmap, &full_x[sx],
+                                        (kb * T::kSteps + j) * T::kSlabElems, m0);
+                    }
+                } else {
+                    // 16-byte pieces of the real token rows straight into the 32-byte
+                    // swizzled slabs the MMA reads (16-byte chunk h of row m sits at
+                    // chunk h ^ ((m >> 2) & 1)); rows past M are never read back.
+                    const int64_t kbyte0 = (int64_t)kb * kKB * T::kXElem;
+                    const int pieces = tok_rows * C::kChunksPerRow;
+                    for (int e = lane; e < pieces; e += 32) {
+                        const int m = e / C::kChunksPerRow;
+                        const int c = e - m * C::kChunksPerRow;
+                        const int64_t kbyte = kbyte0 + 16 * c;
+                        const bool valid = kbyte < p.x_pitch_bytes;
+                        const uint8_t* src = valid ? p.x + (int64_t)(m0 + m) * p.x_pitch_bytes + kbyte : p.x;
+                        uint8_t* d = xs + (c >> 1) * C::kSlabBytes + m * 32 + (((c & 1) ^ ((m >> 2) & 1)) << 4);
+                        cp_async_16_zfill(d, src, valid);
+                    }
+                    cp_async_mbar_arrive_noinc(&full_x[sx]);
                 }
                 ++issued_x;
                 __syncwarp();
             }
         }
         cp_async_wait_all();
-        if (!ok && lane == 0) {
-            // Let every issued TMA land before the CTA can exit.
-            const uint32_t first = issued_x > (uint32_t)C::kSX ? issued_x - C::kSX : 0u;
-            for (uint32_t j = first; j < issued_x; ++j) mbar_wait_drain(&full_x[j % C::kSX], (j / C::kSX) & 1);
+        if constexpr (C::kXTma) {
+            if (!ok && lane == 0) {
+                // Let every issued TMA land before the CTA can exit.
+                const uint32_t first = issued_x > (uint32_t)C::kSX ? issued_x - C::kSX : 0u;
+                for (uint32_t j = first; j < issued_x; ++j) mbar_wait_drain(&full_x[j % C::kSX], (j / C::kSX) & 1);
+            }
         }
-    } else if (warp == kMmaWarp) {
-        // ---------------------------------------------------------- MMA ----
-        if (lane == 0) {
+    } else if (warp >= kMmaWarp) {
+        // --------------------------------------------------------- MMAs ----
+        // Issuer i (warp kMmaWarp + i, lane 0) takes the k-blocks with
+        // global index it % kIssuers == i and accumulates into D_i.
+        const int issuer = warp - kMmaWarp;
+        if (issuer < C::kIssuers && lane == 0) {
             uint32_t idesc;
             if constexpr (KIND == Kind::F16)
                 idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BT >> 3) << 17) | ((128u >> 4) << 24);
             else  // A = unsigned 8-bit codes, B = signed int8, D = s32
                 idesc = (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(BT >> 3) << 17) | ((128u >> 4) << 24);
+            const uint32_t d_tmem = tmem_base + issuer * BT;
             uint32_t it = 0, n_local = 0;
             bool ok = true;
             for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++n_local) {
                 if (!mbar_wait(acc_empty, (n_local & 1) ^ 1, abort_flag)) break;
                 tc_fence_after();
+                bool first = true;
                 for (int kb = 0; kb < n_kb; ++kb, ++it) {
+                    if ((int)(it % C::kIssuers) != issuer) continue;
                     const int sx = it % C::kSX;
                     const int sa = it % C::kSA;
                     if (!mbar_wait(&full_x[sx], (it / C::kSX) & 1, abort_flag)) { ok = false; break; }
@@ -296,21 +337,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int j = 0; j < T::kSteps; ++j) {
                         const uint64_t bdesc = smem_desc_sw32(xs + j * C::kSlabBytes);
-                        const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
+                        const uint32_t acc = (first && j == 0) ? 0u : 1u;
                         if constexpr (KIND == Kind::F16)
-                            mma_f16_ts(tmem_base, a_col + j * 8, bdesc, idesc, acc);
+                            mma_f16_ts(d_tmem, a_col + j * 8, bdesc, idesc, acc);
                         else
-                            mma_i8_ts(tmem_base, a_col + j * 8, bdesc, idesc, acc);
+                            mma_i8_ts(d_tmem, a_col + j * 8, bdesc, idesc, acc);
                     }
+                    first = false;
                     tc_commit(&empty_x[sx]);
                     tc_commit(&empty_a[sa]);
                 }
                 if (!ok) break;
-                tc_commit(acc_full);
+                if (first)
+                    mbar_arrive(acc_full);  // no k-block of this item: D_i unused
+                else
+                    tc_commit(acc_full);
             }
-            // Wait for every MMA this thread issued before tensor memory is freed.
-            tc_commit(drain);
-            mbar_wait_drain(drain, 0);
+            // Every MMA this thread issued completes before tensor memory is freed.
+            tc_commit(&drain[issuer]);
+            mbar_wait_drain(&drain[issuer], 0);
         }
         __syncwarp();
     } else {
@@ -326,6 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++n_local) {
             const int64_t n0 = (int64_t)(item % p.n_row_tiles) * kRows;
             const int m0 = (item / p.n_row_tiles) * BT;
+            const uint32_t it_item = it;
             for (int kb = 0; kb < n_kb; ++kb, ++it) {
                 const int sw = it % C::kSW;
                 if (!warp_wait(&full_w[sw], (it / C::kSW) & 1, abort_flag)) { ok = false; break; }
@@ -382,6 +428,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
 
             // ------------------------------------------------- epilogue ----
+            // Accumulators that received at least one k-block of this item.
+            const int n_acc = n_kb < C::kIssuers ? n_kb : C::kIssuers;
             if (!warp_wait(acc_full, n_local & 1, abort_flag)) { ok = false; break; }
             tc_fence_after();
             const int64_t n = n0 + row;
@@ -391,8 +439,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c0 = 16 * half; c0 < BT; c0 += 32) {
                 if (m0 + c0 >= p.M) break;  // warp-uniform
                 uint32_t v[16];
-                tmem_ld16(tmem_base + lane_base + c0, v);
+                tmem_ld16(tmem_base + lane_base + ((it_item % C::kIssuers) * BT) + c0, v);
                 tmem_wait_ld();
+                float accf[16];
+                int acci[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    accf[j] = __uint_as_float(v[j]);
+                    acci[j] = (int)v[j];
+                }
+                for (int a = 1; a < n_acc; ++a) {
+                    const int d_i = (it_item + a) % C::kIssuers;
+                    tmem_ld16(tmem_base + lane_base + d_i * BT + c0, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        accf[j] = __fadd_rn(accf[j], __uint_as_float(v[j]));
+                        acci[j] += (int)v[j];
+                    }
+                }
                 if (n < p.N) {
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
@@ -400,9 +465,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (m >= p.M) break;
                         float yv;
                         if constexpr (KIND == Kind::F16) {
-                            yv = __fmul_rn(__uint_as_float(v[j]), p.scale);
+                            yv = __fmul_rn(accf[j], p.scale);
                         } else {
-                            const int acc_i = (int)v[j] - 2 * __ldg(p.rowsum + m);
+                            const int acc_i = acci[j] - 2 * __ldg(p.rowsum + m);
                             if (p.acc_out) p.acc_out[(int64_t)m * p.N + n] = acc_i;
                             const float f = __fmul_rn(p.scale, __ldg(p.s_x + m));
                             yv = __fmul_rn((float)acc_i, f);
@@ -496,6 +561,8 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     // k-blocks covering the activation extent (slabs past it are zero-filled by TMA)
     prm.n_kb = (int)((a.KP * kPerWord + kKB - 1) / kKB);
     prm.vec16 = (a.KP % 4 == 0) && (reinterpret_cast<uintptr_t>(a.packed) % 16 == 0);
+    prm.x = static_cast<const uint8_t*>(a.x);
+    prm.x_pitch_bytes = a.x_pitch * T::kXElem;
     prm.scale = a.scale;
     prm.bias = static_cast<const __nv_bfloat16*>(a.bias);
     prm.y = a.y;
