@@ -86,8 +86,9 @@ size_t pn_linear_workspace_size(int kind, int64_t M, int64_t N, int64_t K);
  * bias: NULL or N bf16 values.  y_dtype PN_BF16 reproduces the reference's
  * rounding (bf16(acc*scale), then bf16(. + bf16(bias)), penta_kernel.py:224,
  * :275-276); PN_F32 returns the unrounded fp32 value acc*scale + bias.
- * Workspace: pn_linear_workspace_size(PN_BF16, M, N, K) bytes, zero-filled once
- * before its first use (the kernels leave it zeroed). */
+ * Workspace: pn_linear_workspace_size(PN_BF16, M, N, K) bytes, 16-byte aligned
+ * (non-zero for M <= 64: the activations re-laid-out for the decode kernel);
+ * its contents need no initialisation. */
 int pn_linear_bf16(const void *x, int64_t M, int64_t K, const int32_t *packed, int64_t N, int64_t K_packs,
                    float scale, const void *bias, void *y, int y_dtype, void *workspace,
                    size_t workspace_bytes, void *stream);

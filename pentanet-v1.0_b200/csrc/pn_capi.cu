@@ -178,7 +178,9 @@ int pn_linear_bf16(const void* x, int64_t M, int64_t K, const int32_t* packed, i
     a.y_dtype = y_dtype;
     a.workspace = workspace;
     a.workspace_bytes = workspace_bytes;
-    if (K % 8 != 0 || !aligned(x, 16)) {
+    // Decode-sized M reads x with plain loads (any K); larger M loads it by TMA,
+    // which needs 16-byte rows.
+    if (M > 64 && (K % 8 != 0 || !aligned(x, 16))) {
         cudaError_t e = pn::launch_linear_simt_bf16(a, (cudaStream_t)stream);
         return e == cudaSuccess ? ok() : cuda_fail(e, "pn_linear_bf16 (cuda-core)");
     }

@@ -69,25 +69,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // 1965 MHz boost clock, longer at lower clocks).  Healthy waits last
 // microseconds; a wait that reaches the limit means a producer is gone.
 constexpr long long kWaitLimitCycles = 1ll << 32;
-// Spins between two checks of the abort flag and the cycle counter (the
-// checks stay off the fast path of a wait that completes quickly).
-constexpr uint32_t kSpinsPerCheck = 64;
 
 // Bounded wait.  Returns false (and records PN_ERR_TIMEOUT) when the limit is
 // reached or another thread of the CTA has already aborted (*abort != 0).
+// A wait that does not complete at once backs off with nanosleep (8 ns doubling
+// to 256 ns) so that waiting warps leave the issue slots to working ones.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
-    uint32_t spins = 0;
+    uint32_t ns = 8;
     while (true) {
+        __nanosleep(ns);
         if (mbar_try_wait(bar, parity)) return true;
-        if (++spins % kSpinsPerCheck == 0) {
-            if (*abort) return false;
-            if (clock64() - t0 > kWaitLimitCycles) {
-                *abort = 1;
-                record_status(PN_ERR_TIMEOUT);
-                return false;
-            }
+        if (ns < 256) ns <<= 1;
+        if (*abort) return false;
+        if (clock64() - t0 > kWaitLimitCycles) {
+            *abort = 1;
+            record_status(PN_ERR_TIMEOUT);
+            return false;
         }
     }
 }
@@ -128,6 +127,25 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
         " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
         : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+// Non-tensor bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -191,6 +209,18 @@ __device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t (&v)[4])
     asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(v[0]),
                  "r"(v[1]), "r"(v[2]), "r"(v[3])
                  : "memory");
+}
+__device__ __forceinline__ void tmem_st2(uint32_t taddr, const uint32_t (&v)[2]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1, %2};" ::"r"(taddr), "r"(v[0]), "r"(v[1])
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15, %16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
 }
 // Each thread loads 16 consecutive 32-bit columns of its own lane.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {

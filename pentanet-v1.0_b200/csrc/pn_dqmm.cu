@@ -26,6 +26,7 @@
 #include "pn_common.cuh"
 #include "pn_internal.h"
 
+#include <cstring>
 #include <mutex>
 
 namespace pn {
@@ -35,11 +36,13 @@ constexpr int kWordsPerKB = 16;    // packed words per row per k-block (160 k)
 constexpr int kKB = kWordsPerKB * kPerWord;
 constexpr int kWPitch = 20;        // staged words per row (16 + 4 pad: conflict-free 128-bit reads)
 constexpr int kWStageBytes = kRows * kWPitch * 4;
-constexpr int kUnpackWarps = 8;    // warps 0-7: unpack + epilogue (two per TMEM lane quarter)
-constexpr int kLoadWarp = 8;       // cp.async weight/activation staging (+ activation TMA for large tiles)
-constexpr int kMmaWarp = 9;        // TMEM allocation + MMA issue; warps 9.. issue MMAs
-constexpr int kMaxIssuers = 4;
-constexpr int kThreads = 32 * (kUnpackWarps + 1 + kMaxIssuers);
+constexpr int kUnpackWarps = 16;   // warps 0-15: unpack + epilogue (four per TMEM lane quarter)
+constexpr int kUnpackGroups = kUnpackWarps / 4;  // warps per lane quarter; they take turns on k-blocks
+constexpr int kLoadWarp = kUnpackWarps;       // weight staging
+constexpr int kXLoadWarp = kUnpackWarps + 1;  // activation staging
+constexpr int kMmaWarp = kUnpackWarps + 2;    // TMEM allocation + MMA issue; warps kMmaWarp.. issue MMAs
+constexpr int kMaxIssuers = 2;
+constexpr int kThreads = 32 * (kUnpackWarps + 2 + kMaxIssuers);
 constexpr int kTmemCols = 512;
 
 enum class Kind { F16, I8 };
@@ -70,23 +73,32 @@ struct Cfg {
     // cycles, which small-N MMAs cannot hide.  Large tiles (prefill): TMA boxes
     // and one issuer.
     static constexpr bool kXTma = BT >= 128;
-    static constexpr int kIssuers = BT <= 32 ? 4 : (BT <= 64 ? 2 : 1);
+    // bf16 decode tiles use the permuted unpack; their activations come
+    // pre-arranged (permute_x_kernel) and are staged with one bulk copy per k-block.
+    static constexpr bool kPerm = KIND == Kind::F16 && BT <= 64;
+    static constexpr int kIssuers = BT <= 64 ? 2 : 1;
     static constexpr int kSlabBytes = BT * 32;
     static constexpr int kXStageBytes = kSlabBytes * T::kSteps;
     static constexpr int kChunksPerRow = kKB * T::kXElem / 16;      // 16-byte pieces of one row per k-block
     static constexpr int kDCols = kIssuers * BT;                  // accumulators D_0..D_{kIssuers-1}
     static constexpr int kA0 = kDCols < 32 ? 32 : kDCols;         // first A column
-    static constexpr int kSA = (kTmemCols - kA0) / T::kACols > 6 ? 6 : (kTmemCols - kA0) / T::kACols;
+    // Ring depths.  Waiters that take turns on k-blocks (unpack groups on the
+    // TMEM operand ring and the weight ring, MMA issuers on the operand and
+    // activation rings) must each see every phase of the slots they use, in
+    // order; otherwise a parity wait can pass on a phase two rounds old.  So
+    // each ring depth is a multiple of the number of parties taking turns on it.
+    static constexpr int kSAfit = (kTmemCols - kA0) / T::kACols;
+    static constexpr int kSA = (kSAfit >= 8 ? 8 : kSAfit) / kUnpackGroups * kUnpackGroups;
     static constexpr int kBudget = 200 * 1024;
-    // X ring gets what the W ring (8 stages for small tiles) leaves.
-    static constexpr int kSW = kXStageBytes >= 40 * 1024 ? 4 : (kXStageBytes >= 20 * 1024 ? 6 : 8);
-    static constexpr int kSXraw = (kBudget - kSW * kWStageBytes) / kXStageBytes;
-    static constexpr int kSX = kSXraw > 8 ? 8 : kSXraw;
+    static constexpr int kSW = kXStageBytes >= 40 * 1024 ? 4 : 8;
+    static constexpr int kSXfit = (kBudget - kSW * kWStageBytes) / kXStageBytes;
+    static constexpr int kSX = (kSXfit > 8 ? 8 : kSXfit) / kIssuers * kIssuers;
     static constexpr int kBarOff = kSX * kXStageBytes + kSW * kWStageBytes;
     static constexpr int kNumBars = 2 * kSW + 2 * kSX + 2 * kSA + 3 + kIssuers;
     static constexpr int kSmem = kBarOff + kNumBars * 8 + 16 + 1024;  // + tmem slot/abort flag + align slack
-    static_assert(kSX >= 2, "activation ring too shallow");
-    static_assert(kSA >= 2, "TMEM operand ring too shallow");
+    static_assert(kSX >= 2 && kSX % kIssuers == 0, "activation ring");
+    static_assert(kSA >= kUnpackGroups && kSA % kUnpackGroups == 0 && kSA % kIssuers == 0, "TMEM operand ring");
+    static_assert(kSW % kUnpackGroups == 0, "weight ring");
     static_assert(kA0 + kSA * T::kACols <= kTmemCols, "TMEM over-subscribed");
     static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "token tile");
 };
@@ -96,9 +108,10 @@ struct DqmmParams {
     int64_t N, KP;
     int M;
     int n_row_tiles, n_items, n_kb;
-    int vec16;  // packed rows 16-byte aligned: stage with 16-byte cp.async
-    const uint8_t* x;     // activations (cp.async path): bf16 or int8 rows of x_pitch_bytes
-    int64_t x_pitch_bytes;
+    int w_mode;     // weight staging: 0 TMA box, 1 bulk copies of aligned row segments, 2 cp.async
+    int x_mode;     // activation staging: 0 one 3D TMA box per k-block, 1 one 2D box per MMA K-step
+    const uint8_t* xperm;  // permuted activation slabs (bf16 decode tiles)
+    int64_t packed_bytes;
     float scale;
     const __nv_bfloat16* bias;
     void* y;
@@ -124,6 +137,35 @@ __device__ __forceinline__ void unpack_word_bf16(uint32_t p, uint32_t* r) {
     r[2] = bf16_pair(p >> 12, p << 1);
     r[3] = bf16_pair(p >> 18, p >> 5);
     r[4] = bf16_pair(p >> 24, p >> 11);
+}
+
+// Decode variant: five bf16x2 registers per word in a permuted k order with
+// power-of-two scales, built from two right shifts, one left shift (an IMAD,
+// off the ALU pipe) and five mask-merges -- 0.7 ALU operations per weight
+// instead of ~2.  Register j holds codes j (low half) and j+5 (high half):
+// position 2j <- code j, position 2j+1 <- code j+5 of the word, and the value
+// stored at position q is (c - 2) * 2^kPermExp(q).  The activations are
+// permuted and scaled by 2^-kPermExp(q) to match (permute_x_kernel), so every
+// product is unchanged.
+__host__ __device__ constexpr int perm_src(int q) { return (q & 1) ? (q >> 1) + 5 : (q >> 1); }
+__host__ __device__ constexpr int perm_exp(int q) {
+    return (int)((0x3401340101ull >> (4 * q)) & 0xF);  // {1,0,1,0,4,3,1,0,4,3}
+}
+__device__ __forceinline__ uint32_t bf16_sub2(uint32_t t, uint32_t c) {
+    uint32_t r;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(t), "r"(c));
+    return r;
+}
+__device__ __forceinline__ void unpack_word_bf16_perm(uint32_t p, uint32_t* r) {
+    const uint32_t l1 = p * 2u;  // IMAD, not a shift
+    const uint32_t r2 = p >> 2;
+    const uint32_t r8 = p >> 8;
+    // (code j at bit o_lo, code j+5 at bit 16+o_hi) | bf16 128.0 in both halves
+    r[0] = bf16_sub2((l1 & 0x0007000Eu) | 0x43004300u, 0x43024304u);  // 132 lo, 130 hi
+    r[1] = bf16_sub2((r2 & 0x0007000Eu) | 0x43004300u, 0x43024304u);
+    r[2] = bf16_sub2((r2 & 0x00380070u) | 0x43004300u, 0x43104320u);  // 160 lo, 144 hi
+    r[3] = bf16_sub2((r8 & 0x0007000Eu) | 0x43004300u, 0x43024304u);
+    r[4] = bf16_sub2((r8 & 0x00380070u) | 0x43004300u, 0x43104320u);
 }
 
 // Unsigned codes of two packed words (20 weights) as five int8x4 registers in
@@ -170,7 +212,8 @@ __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) 
 
 template <Kind KIND, int BT>
 __global__ void __launch_bounds__(kThreads, 1)
-    dqmm_kernel(const __grid_constant__ CUtensorMap xmap, const DqmmParams p) {
+    dqmm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                const DqmmParams p) {
     using C = Cfg<KIND, BT>;
     using T = typename C::T;
     extern __shared__ uint8_t smem_raw[];
@@ -196,14 +239,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kSW; ++s) {
             mbar_init(&full_w[s], 32);
-            mbar_init(&empty_w[s], kUnpackWarps);
+            mbar_init(&empty_w[s], 4);
         }
         for (int s = 0; s < C::kSX; ++s) {
-            mbar_init(&full_x[s], C::kXTma ? 1 : 32);
+            mbar_init(&full_x[s], 1);
             mbar_init(&empty_x[s], 1);
         }
         for (int s = 0; s < C::kSA; ++s) {
-            mbar_init(&full_a[s], kUnpackWarps);
+            mbar_init(&full_a[s], 4);
             mbar_init(&empty_a[s], 1);
         }
         mbar_init(acc_full, C::kIssuers);
@@ -216,9 +259,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
-    if constexpr (C::kXTma) {
-        if (warp == kLoadWarp && lane == 0) tma_prefetch_desc(&xmap);
-    }
+    if (warp == kLoadWarp && lane == 0 && p.w_mode == 0) tma_prefetch_desc(&wmap);
+    if (warp == kXLoadWarp && lane == 0 && p.x_mode != 2) tma_prefetch_desc(&xmap);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -227,31 +269,62 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n_kb = p.n_kb;
 
     if (warp == kLoadWarp) {
-        // ------------------------------------------------------- loader ----
+        // ------------------------------------------------ weight loader ----
         uint32_t it = 0;
         bool ok = true;
-        uint32_t issued_x = 0;
         for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
             const int64_t n0 = (int64_t)(item % p.n_row_tiles) * kRows;
             const int m0 = (item / p.n_row_tiles) * BT;
             const int64_t rows_left = p.N - n0;
-            const int tok_rows = p.M - m0 < BT ? p.M - m0 : BT;  // real token rows of this tile
             for (int kb = 0; kb < n_kb; ++kb, ++it) {
                 const int sw = it % C::kSW;
                 if (!warp_wait(&empty_w[sw], ((it / C::kSW) & 1) ^ 1, abort_flag)) { ok = false; break; }
                 uint32_t* dst = smem_w + sw * (kRows * kWPitch);
                 const int64_t g0 = (int64_t)kb * kWordsPerKB;
-                if (p.vec16) {
-                    // 128 rows x 4 chunks of 16 bytes; K_packs % 4 == 0 keeps chunks whole and aligned
-                    const int q = lane & 3;
-                    const bool gvalid = g0 + 4 * q < p.KP;
-                    const int32_t* src = p.packed + (n0 + (lane >> 2)) * p.KP + g0 + 4 * q;
-#pragma unroll 4
-                    for (int j = 0; j < kRows / 8; ++j) {
-                        const int r = (lane >> 2) + 8 * j;
-                        const bool valid = gvalid && r < rows_left;
-                        cp_async_16_zfill(dst + r * kWPitch + 4 * q, valid ? src + (int64_t)8 * j * p.KP : p.packed,
-                                          valid);
+                if (p.w_mode == 0) {
+                    // one box: 128 rows x 16 words, 64-byte swizzled; words >= K_packs
+                    // and rows >= N are zero-filled
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(&full_w[sw], kRows * kWordsPerKB * 4);
+                        tma_load_2d(dst, &wmap, &full_w[sw], (int)g0, (int)n0);
+                    } else {
+                        mbar_arrive(&full_w[sw]);
+                    }
+                } else if (p.w_mode == 1) {
+                    // Row segments start at any word: copy the 16-byte-aligned span
+                    // around each (<= 80 bytes); the unpacker skips the lead-in words.
+                    // A span that would run past the end of the array is copied word
+                    // by word instead.
+                    const int64_t seg = (p.KP - g0) < kWordsPerKB ? (p.KP - g0) : kWordsPerKB;
+                    const uint8_t* base = reinterpret_cast<const uint8_t*>(p.packed);
+                    uint32_t bytes = 0;
+#pragma unroll
+                    for (int j = 0; j < kRows / 32; ++j) {
+                        const int r = lane + 32 * j;
+                        if (r < rows_left) {
+                            const int64_t sb = ((n0 + r) * p.KP + g0) * 4;
+                            const int64_t a0 = sb & ~int64_t(15);
+                            const int64_t a1 = (sb + seg * 4 + 15) & ~int64_t(15);
+                            if (a1 <= p.packed_bytes) bytes += (uint32_t)(a1 - a0);
+                        }
+                    }
+                    mbar_expect_tx(&full_w[sw], bytes);
+#pragma unroll
+                    for (int j = 0; j < kRows / 32; ++j) {
+                        const int r = lane + 32 * j;
+                        if (r < rows_left) {
+                            const int64_t sb = ((n0 + r) * p.KP + g0) * 4;
+                            const int64_t a0 = sb & ~int64_t(15);
+                            const int64_t a1 = (sb + seg * 4 + 15) & ~int64_t(15);
+                            if (a1 <= p.packed_bytes) {
+                                bulk_load(dst + r * kWPitch, base + a0, (uint32_t)(a1 - a0), &full_w[sw]);
+                            } else {
+                                const int off = (int)((sb - a0) >> 2);
+                                for (int w = 0; w < seg; ++w)
+                                    cp_async_4_zfill(dst + r * kWPitch + off + w, p.packed + (n0 + r) * p.KP + g0 + w,
+                                                     true);
+                            }
+                        }
                     }
                 } else {
                     const int wd = lane & 15;
@@ -265,47 +338,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                                          valid);
                     }
                 }
-                cp_async_mbar_arrive_noinc(&full_w[sw]);
+                if (p.w_mode != 0) cp_async_mbar_arrive_noinc(&full_w[sw]);
 
+            }
+        }
+        cp_async_wait_all();
+        if (!ok && lane == 0) {
+            // Let every issued copy land before the CTA can exit.
+            const uint32_t first_w = it > (uint32_t)C::kSW ? it - C::kSW : 0u;
+            for (uint32_t j = first_w; j < it; ++j) mbar_wait_drain(&full_w[j % C::kSW], (j / C::kSW) & 1);
+        }
+    } else if (warp == kXLoadWarp) {
+        // -------------------------------------------- activation loader ----
+        uint32_t it = 0;
+        bool ok = true;
+        for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
+            const int m0 = (item / p.n_row_tiles) * BT;
+            for (int kb = 0; kb < n_kb; ++kb, ++it) {
                 const int sx = it % C::kSX;
                 if (!warp_wait(&empty_x[sx], ((it / C::kSX) & 1) ^ 1, abort_flag)) { ok = false; break; }
                 uint8_t* xs = smem_x + sx * C::kXStageBytes;
-                if constexpr (C::kXTma) {
-                    if (lane == 0) {
-                        mbar_arrive_expect_tx(&full_x[sx], C::kXStageBytes);
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full_x[sx], C::kXStageBytes);
+                    if constexpr (C::kPerm) {
+                        bulk_load(xs, p.xperm + (size_t)kb * C::kXStageBytes, C::kXStageBytes, &full_x[sx]);
+                    } else if (p.x_mode == 0) {
+                        // [slab][row][32 bytes] in one box
+                        tma_load_3d(xs, &xmap, &full_x[sx], 0, m0, kb * T::kSteps);
+                    } else {
 #pragma unroll
                         for (int j = 0; j < T::kSteps; ++j)
                             tma_load_2d(xs + j * C::kSlabBytes, &xmap, &full_x[sx],
                                         (kb * T::kSteps + j) * T::kSlabElems, m0);
                     }
-                } else {
-                    // 16-byte pieces of the real token rows straight into the 32-byte
-                    // swizzled slabs the MMA reads (16-byte chunk h of row m sits at
-                    // chunk h ^ ((m >> 2) & 1)); rows past M are never read back.
-                    const int64_t kbyte0 = (int64_t)kb * kKB * T::kXElem;
-                    const int pieces = tok_rows * C::kChunksPerRow;
-                    for (int e = lane; e < pieces; e += 32) {
-                        const int m = e / C::kChunksPerRow;
-                        const int c = e - m * C::kChunksPerRow;
-                        const int64_t kbyte = kbyte0 + 16 * c;
-                        const bool valid = kbyte < p.x_pitch_bytes;
-                        const uint8_t* src = valid ? p.x + (int64_t)(m0 + m) * p.x_pitch_bytes + kbyte : p.x;
-                        uint8_t* d = xs + (c >> 1) * C::kSlabBytes + m * 32 + (((c & 1) ^ ((m >> 2) & 1)) << 4);
-                        cp_async_16_zfill(d, src, valid);
-                    }
-                    cp_async_mbar_arrive_noinc(&full_x[sx]);
                 }
-                ++issued_x;
                 __syncwarp();
             }
         }
-        cp_async_wait_all();
-        if constexpr (C::kXTma) {
-            if (!ok && lane == 0) {
-                // Let every issued TMA land before the CTA can exit.
-                const uint32_t first = issued_x > (uint32_t)C::kSX ? issued_x - C::kSX : 0u;
-                for (uint32_t j = first; j < issued_x; ++j) mbar_wait_drain(&full_x[j % C::kSX], (j / C::kSX) & 1);
-            }
+        if (!ok && lane == 0) {
+            // Let every issued copy land before the CTA can exit.
+            const uint32_t first = it > (uint32_t)C::kSX ? it - C::kSX : 0u;
+            for (uint32_t j = first; j < it; ++j) mbar_wait_drain(&full_x[j % C::kSX], (j / C::kSX) & 1);
         }
     } else if (warp >= kMmaWarp) {
         // --------------------------------------------------------- MMAs ----
@@ -360,10 +433,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else {
         // ---------------------------------------------- unpack + epilogue ----
-        // Warps q and q+4 share TMEM lane quarter q (rows 32q..32q+31); warp
-        // half h takes words [8h, 8h+8) of every 16-word k-block.
+        // Warps q, q+4, q+8, q+12 share TMEM lane quarter q (rows 32q..32q+31)
+        // and take turns: warp group h unpacks the k-blocks with global index
+        // it % kUnpackGroups == h, all 16 words of its rows.
         const int quarter = warp & 3;
-        const int half = warp >> 2;
+        const int half = warp >> 2;  // warp group within the quarter
         const int row = quarter * 32 + lane;
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         uint32_t it = 0, n_local = 0;
@@ -372,32 +446,72 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int64_t n0 = (int64_t)(item % p.n_row_tiles) * kRows;
             const int m0 = (item / p.n_row_tiles) * BT;
             const uint32_t it_item = it;
+            const int w_off = p.w_mode == 1 ? (int)(((n0 + row) * p.KP) & 3) : 0;
             for (int kb = 0; kb < n_kb; ++kb, ++it) {
+                if ((int)(it % kUnpackGroups) != half) continue;
                 const int sw = it % C::kSW;
                 if (!warp_wait(&full_w[sw], (it / C::kSW) & 1, abort_flag)) { ok = false; break; }
-                const uint4* src =
-                    reinterpret_cast<const uint4*>(smem_w + sw * (kRows * kWPitch) + row * kWPitch + 8 * half);
-                uint32_t wv[8];
+                // The stage is read in two halves of 8 words; the slot is released
+                // once both are in registers.
+                const uint32_t* stage = smem_w + sw * (kRows * kWPitch);
+                auto load8 = [&](int hh, uint32_t (&wv)[8]) {
+                    if (p.w_mode == 0) {
+                        // 64-byte swizzle: 16-byte chunk q of row r sits at chunk q ^ ((r >> 1) & 3)
+                        const uint4* rowp = reinterpret_cast<const uint4*>(stage + row * kWordsPerKB);
 #pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    const uint4 v = src[q];
-                    wv[4 * q + 0] = v.x;
-                    wv[4 * q + 1] = v.y;
-                    wv[4 * q + 2] = v.z;
-                    wv[4 * q + 3] = v.w;
-                }
+                        for (int q = 0; q < 2; ++q) {
+                            const uint4 v = rowp[(2 * hh + q) ^ ((row >> 1) & 3)];
+                            wv[4 * q + 0] = v.x;
+                            wv[4 * q + 1] = v.y;
+                            wv[4 * q + 2] = v.z;
+                            wv[4 * q + 3] = v.w;
+                        }
+                    } else {
+                        // w_mode 1 copies from the 16-byte boundary below the row segment
+                        const uint32_t* rowp = stage + row * kWPitch + w_off + 8 * hh;
+#pragma unroll
+                        for (int w = 0; w < 8; ++w) wv[w] = rowp[w];
+                    }
+                };
+                uint32_t wa[8], wb[8];
+                load8(0, wa);
+                load8(1, wb);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty_w[sw]);
 
                 const int sa = it % C::kSA;
                 if (!warp_wait(&empty_a[sa], ((it / C::kSA) & 1) ^ 1, abort_flag)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t a_addr = tmem_base + lane_base + C::kA0 + sa * T::kACols + half * (T::kACols / 2);
+                const uint32_t a_addr = tmem_base + lane_base + C::kA0 + sa * T::kACols;
                 if constexpr (KIND == Kind::F16) {
-                    // 8 words -> 40 columns
+                    // 16 words -> 80 columns, in two halves of 8 words / 40 columns
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        uint32_t cols[40];
+#pragma unroll
+                        for (int w = 0; w < 8; ++w) {
+                            const uint32_t word = hh ? wb[w] : wa[w];
+                            if constexpr (C::kPerm)
+                                unpack_word_bf16_perm(word, &cols[5 * w]);
+                            else
+                                unpack_word_bf16(word, &cols[5 * w]);
+                        }
+#pragma unroll
+                        for (int c = 0; c < 5; ++c) {
+                            uint32_t v8[8];
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) v8[i] = cols[8 * c + i];
+                            tmem_st8(a_addr + 40 * hh + 8 * c, v8);
+                        }
+                    }
+                } else {
+                    // 8 word pairs -> 40 columns
                     uint32_t cols[40];
 #pragma unroll
-                    for (int w = 0; w < 8; ++w) unpack_word_bf16(wv[w], &cols[5 * w]);
+                    for (int w = 0; w < 4; ++w) {
+                        unpack_pair_u8(wa[2 * w], wa[2 * w + 1], &cols[5 * w]);
+                        unpack_pair_u8(wb[2 * w], wb[2 * w + 1], &cols[20 + 5 * w]);
+                    }
 #pragma unroll
                     for (int c = 0; c < 5; ++c) {
                         uint32_t v8[8];
@@ -405,20 +519,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int i = 0; i < 8; ++i) v8[i] = cols[8 * c + i];
                         tmem_st8(a_addr + 8 * c, v8);
                     }
-                } else {
-                    // 8 words -> 4 pairs -> 20 columns
-                    uint32_t cols[20];
-#pragma unroll
-                    for (int w = 0; w < 4; ++w) unpack_pair_u8(wv[2 * w], wv[2 * w + 1], &cols[5 * w]);
-#pragma unroll
-                    for (int c = 0; c < 2; ++c) {
-                        uint32_t v8[8];
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) v8[i] = cols[8 * c + i];
-                        tmem_st8(a_addr + 8 * c, v8);
-                    }
-                    uint32_t v4[4] = {cols[16], cols[17], cols[18], cols[19]};
-                    tmem_st4(a_addr + 16, v4);
                 }
                 tmem_wait_st();
                 tc_fence_before();
@@ -436,7 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float bias_f = 0.0f;
             if (p.bias != nullptr && n < p.N) bias_f = __bfloat162float(p.bias[n]);
 #pragma unroll 1
-            for (int c0 = 16 * half; c0 < BT; c0 += 32) {
+            for (int c0 = 16 * half; c0 < BT; c0 += 16 * kUnpackGroups) {
                 if (m0 + c0 >= p.M) break;  // warp-uniform
                 uint32_t v[16];
                 tmem_ld16(tmem_base + lane_base + ((it_item % C::kIssuers) * BT) + c0, v);
@@ -497,6 +597,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kMmaWarp) tmem_dealloc(tmem_base, kTmemCols);
 }
 
+// Writes the activations of a bf16 decode tile as the GEMM kernel's shared-
+// memory image of its B operand: per k-block 10 slabs (MMA K-steps) of BT rows
+// x 32 bytes, 32-byte swizzled, each 10-group of k permuted by perm_src and
+// scaled by 2^-perm_exp (exact).  Positions past K are zero; rows >= M are not
+// written (their accumulator columns are never read back).
+template <int BT>
+__global__ void __launch_bounds__(256) permute_x_kernel(const __nv_bfloat16* __restrict__ x, int M, int64_t K,
+                                                        int n_kb, uint8_t* __restrict__ out) {
+    const int64_t kpad = (int64_t)n_kb * kKB;
+    const int64_t total = (int64_t)M * kpad;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        const int m = (int)(idx / kpad);
+        const int64_t kk = idx - (int64_t)m * kpad;
+        const int64_t g = kk / kPerWord;
+        const int q = (int)(kk - g * kPerWord);
+        const int64_t ksrc = g * kPerWord + perm_src(q);
+        float v = ksrc < K ? __bfloat162float(x[(int64_t)m * K + ksrc]) : 0.0f;
+        v = __fmul_rn(v, __int_as_float((127 - perm_exp(q)) << 23));  // * 2^-perm_exp(q), exact
+        const int64_t kb = kk / kKB;
+        const int e = (int)(kk - kb * kKB);
+        const int j = e >> 4;
+        const int ee = e & 15;
+        const int h = (ee >> 3) ^ ((m >> 2) & 1);
+        const size_t off = (size_t)kb * (BT * 32 * 10) + (size_t)j * BT * 32 + m * 32 + h * 16 + (ee & 7) * 2;
+        *reinterpret_cast<__nv_bfloat16*>(out + off) = __float2bfloat16_rn(v);
+    }
+}
+
 // ------------------------------------------------------------------ host ----
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -523,7 +652,14 @@ int device_sm_count() {
     return n;
 }
 
-size_t linear_workspace_bytes(int, int64_t, int64_t, int64_t) { return 0; }
+static int decode_tile(int64_t M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
+
+size_t linear_workspace_bytes(int kind, int64_t M, int64_t, int64_t K) {
+    if (kind != PN_BF16 || M <= 0 || M > 64) return 0;
+    const int64_t KP = (K + kPerWord - 1) / kPerWord;
+    const int64_t n_kb = (KP * kPerWord + kKB - 1) / kKB;
+    return (size_t)(n_kb * decode_tile(M) * 32 * 10);
+}
 
 template <Kind KIND, int BT>
 static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, const char** why) {
@@ -534,21 +670,52 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
         *why = "cuTensorMapEncodeTiled unavailable";
         return PN_ERR_CUDA;
     }
-    // Activations (M, K) with row pitch x_pitch; one box = one 32-byte K-slab of
-    // BT rows, i.e. one MMA K-step.  Columns >= K and rows >= M are zero-filled.
-    CUtensorMap map;
     const int64_t pitch_bytes = a.x_pitch * T::kXElem;
-    cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
-    cuuint64_t strides[1] = {(cuuint64_t)pitch_bytes};
-    cuuint32_t box[2] = {(cuuint32_t)T::kSlabElems, (cuuint32_t)BT};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult cr = encode(&map, KIND == Kind::F16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
-                         2, const_cast<void*>(a.x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (cr != CUDA_SUCCESS) {
-        *why = "cuTensorMapEncodeTiled rejected the activation layout";
-        return PN_ERR_ALIGN;
+    const CUtensorMapDataType xdt = KIND == Kind::F16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    cuuint32_t estr[3] = {1, 1, 1};
+    // Activations.  Preferred: one 3D box per k-block, viewing the rows as
+    // [slab][row][32 bytes] (slab = one MMA K-step), which needs whole slabs
+    // inside the row pitch.  Otherwise one 2D box per slab; columns >= K and
+    // rows >= M are zero-filled either way.
+    CUtensorMap xmap;
+    std::memset(&xmap, 0, sizeof(xmap));
+    int x_mode = 1;
+    const int64_t row_bytes = KIND == Kind::F16 ? a.K * 2 : pitch_bytes;  // bytes the kernel may read per row
+    if (C::kPerm) {
+        x_mode = 2;  // pre-arranged slabs, no tensor map
+    } else if (row_bytes % 32 == 0) {
+        cuuint64_t dims[3] = {(cuuint64_t)T::kSlabElems, (cuuint64_t)a.M, (cuuint64_t)(row_bytes / 32)};
+        cuuint64_t strides[2] = {(cuuint64_t)pitch_bytes, 32};
+        cuuint32_t box[3] = {(cuuint32_t)T::kSlabElems, (cuuint32_t)BT, (cuuint32_t)T::kSteps};
+        if (encode(&xmap, xdt, 3, const_cast<void*>(a.x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+            x_mode = 0;
+    }
+    if (x_mode == 1) {
+        cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
+        cuuint64_t strides[1] = {(cuuint64_t)pitch_bytes};
+        cuuint32_t box[2] = {(cuuint32_t)T::kSlabElems, (cuuint32_t)BT};
+        if (encode(&xmap, xdt, 2, const_cast<void*>(a.x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+            *why = "cuTensorMapEncodeTiled rejected the activation layout";
+            return PN_ERR_ALIGN;
+        }
+    }
+    // Packed weights: one TMA box per k-block when rows are 16-byte aligned.
+    CUtensorMap wmap;
+    std::memset(&wmap, 0, sizeof(wmap));
+    const bool base16 = reinterpret_cast<uintptr_t>(a.packed) % 16 == 0;
+    int w_mode = base16 ? 1 : 2;
+    if (base16 && a.KP % 4 == 0) {
+        cuuint64_t dims[2] = {(cuuint64_t)a.KP, (cuuint64_t)a.N};
+        cuuint64_t strides[1] = {(cuuint64_t)(a.KP * 4)};
+        cuuint32_t box[2] = {(cuuint32_t)kWordsPerKB, (cuuint32_t)kRows};
+        if (encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, const_cast<int32_t*>(a.packed), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+            w_mode = 0;
     }
     DqmmParams prm;
     prm.packed = a.packed;
@@ -558,11 +725,23 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     prm.n_row_tiles = (int)((a.N + kRows - 1) / kRows);
     const int n_tok_tiles = (int)((a.M + BT - 1) / BT);
     prm.n_items = prm.n_row_tiles * n_tok_tiles;
-    // k-blocks covering the activation extent (slabs past it are zero-filled by TMA)
+    // k-blocks covering the packed words (activation slabs past K are zero-filled)
     prm.n_kb = (int)((a.KP * kPerWord + kKB - 1) / kKB);
-    prm.vec16 = (a.KP % 4 == 0) && (reinterpret_cast<uintptr_t>(a.packed) % 16 == 0);
-    prm.x = static_cast<const uint8_t*>(a.x);
-    prm.x_pitch_bytes = a.x_pitch * T::kXElem;
+    prm.w_mode = w_mode;
+    prm.x_mode = x_mode;
+    prm.packed_bytes = a.N * a.KP * 4;
+    prm.xperm = static_cast<const uint8_t*>(a.workspace);
+    if (C::kPerm) {
+        const size_t need = linear_workspace_bytes(PN_BF16, a.M, a.N, a.K);
+        if (a.workspace == nullptr || a.workspace_bytes < need || reinterpret_cast<uintptr_t>(a.workspace) % 16) {
+            *why = "workspace missing, too small or not 16-byte aligned";
+            return PN_ERR_WORKSPACE;
+        }
+        const int64_t total = a.M * (int64_t)prm.n_kb * kKB;
+        const int blocks = (int)((total + 255) / 256 < 1024 ? (total + 255) / 256 : 1024);
+        permute_x_kernel<BT><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(a.x), (int)a.M, a.K, prm.n_kb,
+                                                    static_cast<uint8_t*>(a.workspace));
+    }
     prm.scale = a.scale;
     prm.bias = static_cast<const __nv_bfloat16*>(a.bias);
     prm.y = a.y;
@@ -587,7 +766,7 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     int sms = device_sm_count();
     if (sms <= 0) sms = 148;
     const int grid = prm.n_items < sms ? prm.n_items : sms;
-    kern<<<grid, kThreads, C::kSmem, s>>>(map, prm);
+    kern<<<grid, kThreads, C::kSmem, s>>>(xmap, wmap, prm);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *err = e;
@@ -602,8 +781,13 @@ static int launch_kind(const LinearArgs& a, cudaStream_t s, cudaError_t* err, co
     if (a.M <= 16) return launch_bt<KIND, 16>(a, s, err, why);
     if (a.M <= 32) return launch_bt<KIND, 32>(a, s, err, why);
     if (a.M <= 64) return launch_bt<KIND, 64>(a, s, err, why);
-    if (a.M <= 128) return launch_bt<KIND, 128>(a, s, err, why);
-    return launch_bt<KIND, 256>(a, s, err, why);
+    if constexpr (KIND == Kind::F16) {
+        // bf16 operands of a 256-token tile leave TMEM room for only 3 operand stages
+        return launch_bt<KIND, 128>(a, s, err, why);
+    } else {
+        if (a.M <= 128) return launch_bt<KIND, 128>(a, s, err, why);
+        return launch_bt<KIND, 256>(a, s, err, why);
+    }
 }
 
 int launch_linear(const LinearArgs& a, cudaStream_t s, cudaError_t* err, const char** why) {

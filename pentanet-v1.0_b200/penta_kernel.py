@@ -172,7 +172,7 @@ def penta_linear(x: torch.Tensor, packed_w: torch.Tensor, scale: float, K_orig: 
         assert b.numel() == N
     L = _nat.load()
     ws_bytes = int(L.pn_linear_workspace_size(_nat.PN_BF16, M, N, K))
-    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
     _nat.check(L.pn_linear_bf16(x_2d.data_ptr(), M, K, pw.data_ptr(), N, K_packs, ctypes.c_float(scale),
                                 _nat.ptr(b), y.data_ptr(),
                                 _nat.PN_F32 if out_dtype == torch.float32 else _nat.PN_BF16,
@@ -218,7 +218,7 @@ def penta_linear_i8_prequant(xq: torch.Tensor, s_x: torch.Tensor, rowsum: torch.
     b = bias.detach().to(device=xq.device, dtype=torch.bfloat16).contiguous() if bias is not None else None
     L = _nat.load()
     ws_bytes = int(L.pn_linear_workspace_size(_nat.PN_I8, M, N, K_orig))
-    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=xq.device) if ws_bytes else None
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=xq.device) if ws_bytes else None
     ydt = _nat.PN_F32 if out_dtype == torch.float32 else _nat.PN_BF16
     _nat.check(L.pn_linear_i8(xq.data_ptr(), pitch, s_x.data_ptr(), rowsum.data_ptr(), M, K_orig, pw.data_ptr(),
                               N, K_packs, ctypes.c_float(scale), _nat.ptr(b), _nat.ptr(y), ydt, _nat.ptr(acc),

@@ -77,8 +77,11 @@ def test_tensor_core_shapes(cuda_device, M, N, K):
     _check(x, packed, gamma, w8, K, what=f"M={M} N={N} K={K}")
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 5, 7), (3, 17, 13), (16, 40, 770), (5, 64, 1001), (40, 33, 10)])
-def test_unaligned_k_cuda_core_path(cuda_device, M, N, K):
+@pytest.mark.parametrize("M,N,K", [(1, 5, 7), (3, 17, 13), (16, 40, 770), (5, 64, 1001), (40, 33, 10),
+                                   (100, 20, 13), (70, 8, 1001)])
+def test_unaligned_k(cuda_device, M, N, K):
+    """K not a multiple of 8: decode tiles (M <= 64) re-lay the activations with
+    plain loads; larger M takes the CUDA-core kernel."""
     packed, gamma, w8 = _layer(N, K, seed=N * K, dev=cuda_device, std=0.05)
     x = gen_act(M, K, seed=M * K).to(torch.bfloat16).to(cuda_device)
     _check(x, packed, gamma, w8, K, what=f"simt M={M} N={N} K={K}")
@@ -147,3 +150,18 @@ def test_cfg4_full_size_properties(cuda_device):
 def test_no_device_timeouts(cuda_device):
     import penta_native as nat
     assert nat.device_status(reset=True) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1024, 8192), (16, 640, 3072), (64, 512, 4096), (300, 512, 3072),
+                                   (1000, 260, 768)])
+def test_repeat_calls_bit_identical(cuda_device, M, N, K):
+    """Ring-slot reuse stress: many repeated launches over several tiles must
+    give bit-identical results (a stale-phase race would perturb them)."""
+    packed, gamma, w8 = _layer(N, K, seed=N + K, dev=cuda_device)
+    x = gen_act(M, K, seed=M).to(torch.bfloat16).to(cuda_device)
+    first = pk.penta_linear(x, packed, gamma, K, out_dtype=torch.float32)
+    for _ in range(8):
+        assert torch.equal(pk.penta_linear(x, packed, gamma, K, out_dtype=torch.float32), first)
+    xf = x.float().cpu().numpy()
+    rows = [0, N // 2, N - 1]
+    assert_close(first[:, rows].cpu().numpy(), orc.matmul_f64(xf, w8[rows], gamma), what="repeat")
