@@ -93,6 +93,18 @@ int pn_linear_bf16(const void *x, int64_t M, int64_t K, const int32_t *packed, i
                    float scale, const void *bias, void *y, int y_dtype, void *workspace,
                    size_t workspace_bytes, void *stream);
 
+/* pn_linear_bf16 without a workspace argument, for callers that cannot
+ * allocate device memory (code where no allocator may run, or embeddings that
+ * hand the library only raw input/output pointers).  No counterpart in the
+ * reference (its wrapper allocates with torch.empty, penta_kernel.py:259).
+ * Scratch comes from one static 4 MiB device array per GPU (held until the
+ * process exits); shapes needing more return PN_ERR_WORKSPACE.  Calls that
+ * overlap on the GPU share that array and race: serialise them.  The first
+ * call on a device looks up the array's address; make it before any stream
+ * capture.  Allocates and frees nothing. */
+int pn_linear_bf16_nows(const void *x, int64_t M, int64_t K, const int32_t *packed, int64_t N, int64_t K_packs,
+                        float scale, const void *bias, void *y, int y_dtype, void *stream);
+
 /* ---- int8 activation path: replaces the int8 line of the reference
  *      benchmark (penta_avx2_wrapper.py:130-131,137,147), per token --------- */
 

@@ -10,3 +10,4 @@
 #include "pn_dqmm.cu"
 #include "pn_simt.cu"
 #include "pn_capi.cu"
+#include "pn_static_ws.cu"

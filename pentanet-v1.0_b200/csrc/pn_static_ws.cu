@@ -1,0 +1,77 @@
+// pn_static_ws.cu -- pn_linear_bf16 for callers that cannot allocate device memory.
+//
+// pn_linear_bf16 needs scratch for batches of up to 64 tokens: the activations
+// re-laid-out for the decode kernel, sized by pn_linear_workspace_size.  Some
+// callers have no way to provide it: code that runs where no allocator may be
+// called (a host callback, a signal-safe or real-time path, an embedding that
+// hands the library only raw input/output pointers, or a process whose device
+// memory is fully reserved up front).  pn_linear_bf16_nows serves them from
+// one fixed scratch array that lives in this file as a __device__ variable:
+// every GPU that loads the library holds kStaticScratchBytes of it until the
+// process exits, and no call allocates or frees anything.
+//
+// Limits and sharing:
+//   * the scratch a call needs must be <= kStaticScratchBytes (4 MiB: e.g.
+//     K = 28672 at up to 64 tokens); larger requests are rejected with
+//     PN_ERR_WORKSPACE before anything is enqueued;
+//   * all calls on a device share the one array and it keeps the last call's
+//     contents.  The decode kernel writes every byte it later reads, so nothing
+//     needs clearing between calls -- but calls that can overlap on the GPU
+//     (different streams without ordering between them) race on the array and
+//     must be serialised by the caller;
+//   * the first call on a device looks up the array's device address
+//     (cudaGetSymbolAddress, with that device current) and caches it; make that
+//     first call before any stream capture on the device.
+#include <mutex>
+
+#include "pn_common.cuh"
+#include "pn_internal.h"
+
+namespace pn {
+
+constexpr size_t kStaticScratchBytes = size_t(4) << 20;
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[kMaxDevices] = {};
+
+// Device address of g_static_scratch on the current device (host code cannot
+// use the symbol itself: on the host it names a stand-in, not device memory).
+int static_scratch(void** out, const char** why) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        *why = "no usable current device";
+        return PN_ERR_CUDA;
+    }
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (g_scratch_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            *why = "cudaGetSymbolAddress of the static scratch array failed";
+            return PN_ERR_CUDA;
+        }
+        g_scratch_ptr[dev] = p;
+    }
+    *out = g_scratch_ptr[dev];
+    return PN_OK;
+}
+}  // namespace
+}  // namespace pn
+
+extern "C" int pn_linear_bf16_nows(const void* x, int64_t M, int64_t K, const int32_t* packed, int64_t N,
+                                   int64_t K_packs, float scale, const void* bias, void* y, int y_dtype,
+                                   void* stream) {
+    const size_t need = pn::linear_workspace_bytes(PN_BF16, M, N, K);
+    if (need > pn::kStaticScratchBytes)
+        return fail(PN_ERR_WORKSPACE,
+                    "pn_linear_bf16_nows: this shape needs %zu bytes of scratch; the static array holds %zu "
+                    "(use pn_linear_bf16 with a caller-provided workspace)",
+                    need, pn::kStaticScratchBytes);
+    void* ws = nullptr;
+    const char* why = "";
+    if (const int st = pn::static_scratch(&ws, &why)) return fail(st, "pn_linear_bf16_nows: %s", why);
+    return pn_linear_bf16(x, M, K, packed, N, K_packs, scale, bias, y, y_dtype, ws, pn::kStaticScratchBytes, stream);
+}
