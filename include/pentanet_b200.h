@@ -77,18 +77,29 @@ int pn_unpack(const int32_t *packed, int64_t N, int64_t K_packs, int64_t K_orig,
 /* ---- fused dequant-matmul: replaces penta_linear / _penta_matmul_kernel
  *      (penta_kernel.py:111-278) ------------------------------------------- */
 
-/* Workspace bytes for pn_linear_bf16 / pn_linear_i8 at this shape (0 allowed
- * when the result is 0).  kind: PN_BF16 or PN_I8. */
+/* Recommended workspace bytes for pn_linear_bf16 / pn_linear_i8 at this shape
+ * (0 allowed when the result is 0).  kind: PN_BF16 or PN_I8.  With this much
+ * the kernel may split one output tile's K range over several SMs when there
+ * are few tiles per SM (the partial sums live in the workspace).  A smaller
+ * workspace is accepted down to pn_linear_workspace_min_size; the call then
+ * gives each SM whole tiles. */
 size_t pn_linear_workspace_size(int kind, int64_t M, int64_t N, int64_t K);
 
+/* The least workspace pn_linear_bf16 / pn_linear_i8 accept at this shape
+ * (whole output tiles per SM).  No reference counterpart. */
+size_t pn_linear_workspace_min_size(int kind, int64_t M, int64_t N, int64_t K);
+
 /* Y[M, N] = (X[M, K] . unpack(packed)^T) * scale (+ bias), fp32 accumulation.
- * X: bf16 row-major (row pitch K elements).  packed: (N, K_packs) int32.
+ * X: bf16 row-major (row pitch K elements).  packed: (N, K_packs) int32,
+ * 16-byte aligned.
  * bias: NULL or N bf16 values.  y_dtype PN_BF16 reproduces the reference's
  * rounding (bf16(acc*scale), then bf16(. + bf16(bias)), penta_kernel.py:224,
  * :275-276); PN_F32 returns the unrounded fp32 value acc*scale + bias.
- * Workspace: pn_linear_workspace_size(PN_BF16, M, N, K) bytes, 16-byte aligned
- * (non-zero for M <= 64: the activations re-laid-out for the decode kernel);
- * its contents need no initialisation. */
+ * Workspace: pn_linear_workspace_size(PN_BF16, M, N, K) bytes, 256-byte
+ * aligned, contents need no initialisation (each call sets what it reads, on
+ * its stream).  It holds the activations re-laid out for the decode kernel
+ * (M <= 64), a copy of the packed rows at a 16-byte pitch when
+ * K_packs % 4 != 0, and the partial sums of split tiles. */
 int pn_linear_bf16(const void *x, int64_t M, int64_t K, const int32_t *packed, int64_t N, int64_t K_packs,
                    float scale, const void *bias, void *y, int y_dtype, void *workspace,
                    size_t workspace_bytes, void *stream);

@@ -145,6 +145,10 @@ size_t pn_linear_workspace_size(int kind, int64_t M, int64_t N, int64_t K) {
     return pn::linear_workspace_bytes(kind, M, N, K);
 }
 
+size_t pn_linear_workspace_min_size(int kind, int64_t M, int64_t N, int64_t K) {
+    return pn::linear_workspace_min_bytes(kind, M, N, K);
+}
+
 int pn_linear_bf16(const void* x, int64_t M, int64_t K, const int32_t* packed, int64_t N, int64_t K_packs,
                    float scale, const void* bias, void* y, int y_dtype, void* workspace, size_t workspace_bytes,
                    void* stream) {
@@ -156,11 +160,12 @@ int pn_linear_bf16(const void* x, int64_t M, int64_t K, const int32_t* packed, i
     if (K_packs != k_packs(K))
         return fail(PN_ERR_SHAPE, "pn_linear_bf16: activation K=%lld needs K_packs=%lld, got %lld", (long long)K,
                     (long long)k_packs(K), (long long)K_packs);
-    if (!aligned(x, 2) || !aligned(packed, 4) || !aligned(y, y_dtype == PN_F32 ? 4 : 2) || !aligned(bias, 2))
-        return fail(PN_ERR_ALIGN, "pn_linear_bf16: misaligned pointer");
-    const size_t need = pn::linear_workspace_bytes(PN_BF16, M, N, K);
+    if (!aligned(x, 2) || !aligned(packed, 16) || !aligned(y, y_dtype == PN_F32 ? 4 : 2) || !aligned(bias, 2))
+        return fail(PN_ERR_ALIGN, "pn_linear_bf16: misaligned pointer (packed weights need 16-byte alignment)");
+    const size_t need = pn::linear_workspace_min_bytes(PN_BF16, M, N, K);
     if (need > 0 && (!workspace || workspace_bytes < need))
-        return fail(PN_ERR_WORKSPACE, "pn_linear_bf16: workspace needs %zu bytes", need);
+        return fail(PN_ERR_WORKSPACE, "pn_linear_bf16: workspace needs at least %zu bytes (%zu recommended)", need,
+                    pn::linear_workspace_bytes(PN_BF16, M, N, K));
     if (int st = check_device()) return st;
     if (M == 0 || N == 0) return ok();
     pn::LinearArgs a{};
@@ -220,12 +225,13 @@ int pn_linear_i8(const int8_t* xq, int64_t xq_pitch, const float* s_x, const int
     if (K_packs != k_packs(K))
         return fail(PN_ERR_SHAPE, "pn_linear_i8: K=%lld needs K_packs=%lld, got %lld", (long long)K,
                     (long long)k_packs(K), (long long)K_packs);
-    if (!aligned(xq, 16) || !aligned(packed, 4) || !aligned(s_x, 4) || !aligned(rowsum, 4) || !aligned(acc_out, 4) ||
+    if (!aligned(xq, 16) || !aligned(packed, 16) || !aligned(s_x, 4) || !aligned(rowsum, 4) || !aligned(acc_out, 4) ||
         !aligned(y, y_dtype == PN_F32 ? 4 : 2) || !aligned(bias, 2))
         return fail(PN_ERR_ALIGN, "pn_linear_i8: misaligned pointer");
-    const size_t need = pn::linear_workspace_bytes(PN_I8, M, N, K);
+    const size_t need = pn::linear_workspace_min_bytes(PN_I8, M, N, K);
     if (need > 0 && (!workspace || workspace_bytes < need))
-        return fail(PN_ERR_WORKSPACE, "pn_linear_i8: workspace needs %zu bytes", need);
+        return fail(PN_ERR_WORKSPACE, "pn_linear_i8: workspace needs at least %zu bytes (%zu recommended)", need,
+                    pn::linear_workspace_bytes(PN_I8, M, N, K));
     if (int st = check_device()) return st;
     if (M == 0 || N == 0) return ok();
     pn::LinearArgs a{};

@@ -34,15 +34,16 @@ namespace pn {
 constexpr int kRows = 128;         // weight rows per tile (MMA M, TMEM lanes)
 constexpr int kWordsPerKB = 16;    // packed words per row per k-block (160 k)
 constexpr int kKB = kWordsPerKB * kPerWord;
-constexpr int kWPitch = 20;        // staged words per row (16 + 4 pad: conflict-free 128-bit reads)
-constexpr int kWStageBytes = kRows * kWPitch * 4;
+constexpr int kWStageWords = 2 * kWordsPerKB;           // one weight stage = 2 k-blocks = 128 bytes per row
+constexpr int kWStageBytes = kRows * kWStageWords * 4;  // 16 KB, one 128B-swizzled TMA box
 constexpr int kUnpackWarps = 16;   // warps 0-15: unpack + epilogue (four per TMEM lane quarter)
 constexpr int kUnpackGroups = kUnpackWarps / 4;  // warps per lane quarter; they take turns on k-blocks
-constexpr int kLoadWarp = kUnpackWarps;       // weight staging
-constexpr int kXLoadWarp = kUnpackWarps + 1;  // activation staging
-constexpr int kMmaWarp = kUnpackWarps + 2;    // TMEM allocation + MMA issue; warps kMmaWarp.. issue MMAs
+constexpr int kLoadWarp = kUnpackWarps;       // weight staging, even stages
+constexpr int kLoadWarp2 = kUnpackWarps + 1;  // weight staging, odd stages
+constexpr int kXLoadWarp = kUnpackWarps + 2;  // activation staging
+constexpr int kMmaWarp = kUnpackWarps + 3;    // TMEM allocation + MMA issue; warps kMmaWarp.. issue MMAs
 constexpr int kMaxIssuers = 2;
-constexpr int kThreads = 32 * (kUnpackWarps + 2 + kMaxIssuers);
+constexpr int kThreads = 32 * (kUnpackWarps + 3 + kMaxIssuers);
 constexpr int kTmemCols = 512;
 
 enum class Kind { F16, I8 };
@@ -90,15 +91,16 @@ struct Cfg {
     static constexpr int kSAfit = (kTmemCols - kA0) / T::kACols;
     static constexpr int kSA = (kSAfit >= 8 ? 8 : kSAfit) / kUnpackGroups * kUnpackGroups;
     static constexpr int kBudget = 200 * 1024;
-    static constexpr int kSW = kXStageBytes >= 40 * 1024 ? 4 : 8;
+    static constexpr int kSW = kXStageBytes >= 40 * 1024 ? 4 : (kXStageBytes >= 20 * 1024 ? 6 : 8);
     static constexpr int kSXfit = (kBudget - kSW * kWStageBytes) / kXStageBytes;
     static constexpr int kSX = (kSXfit > 8 ? 8 : kSXfit) / kIssuers * kIssuers;
     static constexpr int kBarOff = kSX * kXStageBytes + kSW * kWStageBytes;
     static constexpr int kNumBars = 2 * kSW + 2 * kSX + 2 * kSA + 3 + kIssuers;
-    static constexpr int kSmem = kBarOff + kNumBars * 8 + 16 + 1024;  // + tmem slot/abort flag + align slack
+    static constexpr int kSmem = kBarOff + kNumBars * 8 + 16 + 1024;  // + tmem slot, abort and last-arriver flags + align slack
     static_assert(kSX >= 2 && kSX % kIssuers == 0, "activation ring");
     static_assert(kSA >= kUnpackGroups && kSA % kUnpackGroups == 0 && kSA % kIssuers == 0, "TMEM operand ring");
-    static_assert(kSW % kUnpackGroups == 0, "weight ring");
+    static_assert(kSW % 2 == 0, "weight ring: two producers, two k-blocks per stage");
+    static_assert((kSX * kXStageBytes) % 1024 == 0, "weight stages must stay 1024-byte aligned (128B swizzle)");
     static_assert(kA0 + kSA * T::kACols <= kTmemCols, "TMEM over-subscribed");
     static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "token tile");
 };
@@ -108,7 +110,11 @@ struct DqmmParams {
     int64_t N, KP;
     int M;
     int n_row_tiles, n_items, n_kb;
-    int w_mode;     // weight staging: 0 TMA box, 1 bulk copies of aligned row segments, 2 cp.async
+    int64_t total_pairs;   // n_items * (n_kb / 2): the flattened (tile, k-block pair) work
+    int unit;              // pairs per indivisible unit: 1 (tiles may split) or n_kb / 2 (whole tiles)
+    uint32_t* partials;    // [gridDim.x][2][128][BT] fp32 / int32 partial accumulators
+    int* counters;         // [n_items][16 unpack warps] arrival counters of split tiles (zeroed by the host)
+    int w_pad;      // weights read from a 16-byte-pitch copy in the workspace (unused by the kernel)
     int x_mode;     // activation staging: 0 one 3D TMA box per k-block, 1 one 2D box per MMA K-step
     const uint8_t* xperm;  // permuted activation slabs (bf16 decode tiles)
     int64_t packed_bytes;
@@ -186,19 +192,6 @@ __device__ __forceinline__ void unpack_pair_u8(uint32_t p0, uint32_t p1, uint32_
     r[4] = spread4(hi >> 16);
 }
 
-__device__ __forceinline__ void cp_async_16_zfill(void* smem_dst, const void* gmem_src, bool valid) {
-    const uint32_t src_size = valid ? 16u : 0u;
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src),
-                 "r"(src_size)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_4_zfill(void* smem_dst, const void* gmem_src, bool valid) {
-    const uint32_t src_size = valid ? 4u : 0u;
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src),
-                 "r"(src_size)
-                 : "memory");
-}
-
 // Bounded wait used while draining after an abort (ignores the abort flag).
 __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
     const long long t0 = clock64();
@@ -208,6 +201,39 @@ __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) 
             return;
         }
     }
+}
+
+// Work split (stream-K style): the flattened (tile, k-block pair) space is cut
+// into gridDim.x equal contiguous ranges of units, one per CTA; a unit is one
+// k-block pair (tiles may split) or one whole tile.  A CTA walks its range as
+// segments -- a whole tile, or the k-block range of one tile that its range
+// covers.  Tiles split over several CTAs are finished by the last one to
+// arrive, which sums the partials in CTA order (deterministic).
+struct Seg {
+    int tile;
+    int kb0, kb1;   // k-blocks [kb0, kb1), both even
+    bool whole;
+};
+__device__ __forceinline__ int64_t range_begin(const DqmmParams& p, int c) {
+    const int64_t units = p.total_pairs / p.unit;
+    return (int64_t)c * units / gridDim.x * p.unit;
+}
+// CTA whose range holds pair u.
+__device__ __forceinline__ int owner_of(const DqmmParams& p, int64_t u) {
+    const int64_t units = p.total_pairs / p.unit;
+    return (int)(((u / p.unit + 1) * (int64_t)gridDim.x - 1) / units);
+}
+__device__ __forceinline__ Seg segment_at(const DqmmParams& p, int64_t u, int64_t u_end) {
+    const int P = p.n_kb / 2;
+    Seg g;
+    g.tile = (int)(u / P);
+    const int pb = (int)(u - (int64_t)g.tile * P);
+    const int64_t left = u_end - u;
+    const int pe = (int64_t)(P - pb) < left ? P : (int)(pb + left);
+    g.kb0 = 2 * pb;
+    g.kb1 = 2 * pe;
+    g.whole = pb == 0 && pe == P;
+    return g;
 }
 
 template <Kind KIND, int BT>
@@ -238,8 +264,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kSW; ++s) {
-            mbar_init(&full_w[s], 32);
-            mbar_init(&empty_w[s], 4);
+            mbar_init(&full_w[s], 1);
+            mbar_init(&empty_w[s], 8);  // 2 k-blocks x 4 lane quarters
         }
         for (int s = 0; s < C::kSX; ++s) {
             mbar_init(&full_x[s], 1);
@@ -259,102 +285,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
-    if (warp == kLoadWarp && lane == 0 && p.w_mode == 0) tma_prefetch_desc(&wmap);
+    if ((warp == kLoadWarp || warp == kLoadWarp2) && lane == 0) tma_prefetch_desc(&wmap);
     if (warp == kXLoadWarp && lane == 0 && p.x_mode != 2) tma_prefetch_desc(&xmap);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    const int n_kb = p.n_kb;
-
-    if (warp == kLoadWarp) {
-        // ------------------------------------------------ weight loader ----
-        uint32_t it = 0;
+    if (warp == kLoadWarp || warp == kLoadWarp2) {
+        // ------------------------------------------------ weight loaders ----
+        // One TMA box per stage: 128 rows x 32 words (2 k-blocks), 128-byte
+        // swizzled; words >= K_packs and rows >= N are zero-filled.  The two
+        // loader warps take alternate stages.
+        const int producer = warp - kLoadWarp;
+        uint32_t st = 0;  // global stage counter
         bool ok = true;
-        for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
-            const int64_t n0 = (int64_t)(item % p.n_row_tiles) * kRows;
-            const int m0 = (item / p.n_row_tiles) * BT;
-            const int64_t rows_left = p.N - n0;
-            for (int kb = 0; kb < n_kb; ++kb, ++it) {
-                const int sw = it % C::kSW;
-                if (!warp_wait(&empty_w[sw], ((it / C::kSW) & 1) ^ 1, abort_flag)) { ok = false; break; }
-                uint32_t* dst = smem_w + sw * (kRows * kWPitch);
-                const int64_t g0 = (int64_t)kb * kWordsPerKB;
-                if (p.w_mode == 0) {
-                    // one box: 128 rows x 16 words, 64-byte swizzled; words >= K_packs
-                    // and rows >= N are zero-filled
-                    if (lane == 0) {
-                        mbar_arrive_expect_tx(&full_w[sw], kRows * kWordsPerKB * 4);
-                        tma_load_2d(dst, &wmap, &full_w[sw], (int)g0, (int)n0);
-                    } else {
-                        mbar_arrive(&full_w[sw]);
-                    }
-                } else if (p.w_mode == 1) {
-                    // Row segments start at any word: copy the 16-byte-aligned span
-                    // around each (<= 80 bytes); the unpacker skips the lead-in words.
-                    // A span that would run past the end of the array is copied word
-                    // by word instead.
-                    const int64_t seg = (p.KP - g0) < kWordsPerKB ? (p.KP - g0) : kWordsPerKB;
-                    const uint8_t* base = reinterpret_cast<const uint8_t*>(p.packed);
-                    uint32_t bytes = 0;
-#pragma unroll
-                    for (int j = 0; j < kRows / 32; ++j) {
-                        const int r = lane + 32 * j;
-                        if (r < rows_left) {
-                            const int64_t sb = ((n0 + r) * p.KP + g0) * 4;
-                            const int64_t a0 = sb & ~int64_t(15);
-                            const int64_t a1 = (sb + seg * 4 + 15) & ~int64_t(15);
-                            if (a1 <= p.packed_bytes) bytes += (uint32_t)(a1 - a0);
-                        }
-                    }
-                    mbar_expect_tx(&full_w[sw], bytes);
-#pragma unroll
-                    for (int j = 0; j < kRows / 32; ++j) {
-                        const int r = lane + 32 * j;
-                        if (r < rows_left) {
-                            const int64_t sb = ((n0 + r) * p.KP + g0) * 4;
-                            const int64_t a0 = sb & ~int64_t(15);
-                            const int64_t a1 = (sb + seg * 4 + 15) & ~int64_t(15);
-                            if (a1 <= p.packed_bytes) {
-                                bulk_load(dst + r * kWPitch, base + a0, (uint32_t)(a1 - a0), &full_w[sw]);
-                            } else {
-                                const int off = (int)((sb - a0) >> 2);
-                                for (int w = 0; w < seg; ++w)
-                                    cp_async_4_zfill(dst + r * kWPitch + off + w, p.packed + (n0 + r) * p.KP + g0 + w,
-                                                     true);
-                            }
-                        }
-                    }
-                } else {
-                    const int wd = lane & 15;
-                    const bool gvalid = g0 + wd < p.KP;
-                    const int32_t* src = p.packed + (n0 + (lane >> 4)) * p.KP + g0 + wd;
-#pragma unroll 8
-                    for (int j = 0; j < kRows / 2; ++j) {
-                        const int r = (lane >> 4) + 2 * j;
-                        const bool valid = gvalid && r < rows_left;
-                        cp_async_4_zfill(dst + r * kWPitch + wd, valid ? src + (int64_t)2 * j * p.KP : p.packed,
-                                         valid);
-                    }
+        const int64_t u_end = range_begin(p, blockIdx.x + 1);
+        for (int64_t u = range_begin(p, blockIdx.x); u < u_end && ok;) {
+            const Seg g = segment_at(p, u, u_end);
+            u += (g.kb1 - g.kb0) / 2;
+            const int n0 = (g.tile % p.n_row_tiles) * kRows;
+            for (int ws = g.kb0 / 2; ws < g.kb1 / 2; ++ws, ++st) {
+                if ((int)(st & 1) != producer) continue;
+                const int sw = st % C::kSW;
+                if (!warp_wait(&empty_w[sw], ((st / C::kSW) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full_w[sw], kWStageBytes);
+                    tma_load_2d(smem_w + sw * (kWStageBytes / 4), &wmap, &full_w[sw], ws * kWStageWords, n0);
                 }
-                if (p.w_mode != 0) cp_async_mbar_arrive_noinc(&full_w[sw]);
-
+                __syncwarp();
             }
         }
-        cp_async_wait_all();
         if (!ok && lane == 0) {
             // Let every issued copy land before the CTA can exit.
-            const uint32_t first_w = it > (uint32_t)C::kSW ? it - C::kSW : 0u;
-            for (uint32_t j = first_w; j < it; ++j) mbar_wait_drain(&full_w[j % C::kSW], (j / C::kSW) & 1);
+            for (uint32_t j = (st > (uint32_t)C::kSW ? st - C::kSW : 0u); j < st; ++j)
+                if ((int)(j & 1) == producer) mbar_wait_drain(&full_w[j % C::kSW], (j / C::kSW) & 1);
         }
     } else if (warp == kXLoadWarp) {
         // -------------------------------------------- activation loader ----
         uint32_t it = 0;
         bool ok = true;
-        for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
-            const int m0 = (item / p.n_row_tiles) * BT;
-            for (int kb = 0; kb < n_kb; ++kb, ++it) {
+        const int64_t u_end = range_begin(p, blockIdx.x + 1);
+        for (int64_t u = range_begin(p, blockIdx.x); u < u_end && ok;) {
+            const Seg g = segment_at(p, u, u_end);
+            u += (g.kb1 - g.kb0) / 2;
+            const int m0 = (g.tile / p.n_row_tiles) * BT;
+            for (int kb = g.kb0; kb < g.kb1; ++kb, ++it) {
                 const int sx = it % C::kSX;
                 if (!warp_wait(&empty_x[sx], ((it / C::kSX) & 1) ^ 1, abort_flag)) { ok = false; break; }
                 uint8_t* xs = smem_x + sx * C::kXStageBytes;
@@ -394,11 +370,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t d_tmem = tmem_base + issuer * BT;
             uint32_t it = 0, n_local = 0;
             bool ok = true;
-            for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++n_local) {
+            const int64_t u_end = range_begin(p, blockIdx.x + 1);
+            for (int64_t u = range_begin(p, blockIdx.x); u < u_end && ok; ++n_local) {
+                const Seg g = segment_at(p, u, u_end);
+                u += (g.kb1 - g.kb0) / 2;
                 if (!mbar_wait(acc_empty, (n_local & 1) ^ 1, abort_flag)) break;
                 tc_fence_after();
                 bool first = true;
-                for (int kb = 0; kb < n_kb; ++kb, ++it) {
+                for (int kb = g.kb0; kb < g.kb1; ++kb, ++it) {
                     if ((int)(it % C::kIssuers) != issuer) continue;
                     const int sx = it % C::kSX;
                     const int sa = it % C::kSA;
@@ -442,35 +421,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         uint32_t it = 0, n_local = 0;
         bool ok = true;
-        for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++n_local) {
-            const int64_t n0 = (int64_t)(item % p.n_row_tiles) * kRows;
-            const int m0 = (item / p.n_row_tiles) * BT;
+        const int64_t u_begin = range_begin(p, blockIdx.x);
+        const int64_t u_end = range_begin(p, blockIdx.x + 1);
+        const int my_first_tile = (int)(u_begin / (p.n_kb / 2));
+        for (int64_t u = u_begin; u < u_end && ok; ++n_local) {
+            const Seg g = segment_at(p, u, u_end);
+            u += (g.kb1 - g.kb0) / 2;
+            const int64_t n0 = (int64_t)(g.tile % p.n_row_tiles) * kRows;
+            const int m0 = (g.tile / p.n_row_tiles) * BT;
             const uint32_t it_item = it;
-            const int w_off = p.w_mode == 1 ? (int)(((n0 + row) * p.KP) & 3) : 0;
-            for (int kb = 0; kb < n_kb; ++kb, ++it) {
+            for (int kb = g.kb0; kb < g.kb1; ++kb, ++it) {
                 if ((int)(it % kUnpackGroups) != half) continue;
-                const int sw = it % C::kSW;
-                if (!warp_wait(&full_w[sw], (it / C::kSW) & 1, abort_flag)) { ok = false; break; }
-                // The stage is read in two halves of 8 words; the slot is released
-                // once both are in registers.
-                const uint32_t* stage = smem_w + sw * (kRows * kWPitch);
+                // Weight stages hold 2 k-blocks: global k-block `it` is half (it & 1)
+                // of global stage it / 2 (every item has an even k-block count).
+                const uint32_t wst = it >> 1;
+                const int sw = wst % C::kSW;
+                if (!warp_wait(&full_w[sw], (wst / C::kSW) & 1, abort_flag)) { ok = false; break; }
+                // 128-byte swizzle: 16-byte chunk q of row r sits at chunk q ^ (r & 7).
+                const uint4* rowp = reinterpret_cast<const uint4*>(smem_w + sw * (kWStageBytes / 4) + row * kWStageWords);
                 auto load8 = [&](int hh, uint32_t (&wv)[8]) {
-                    if (p.w_mode == 0) {
-                        // 64-byte swizzle: 16-byte chunk q of row r sits at chunk q ^ ((r >> 1) & 3)
-                        const uint4* rowp = reinterpret_cast<const uint4*>(stage + row * kWordsPerKB);
 #pragma unroll
-                        for (int q = 0; q < 2; ++q) {
-                            const uint4 v = rowp[(2 * hh + q) ^ ((row >> 1) & 3)];
-                            wv[4 * q + 0] = v.x;
-                            wv[4 * q + 1] = v.y;
-                            wv[4 * q + 2] = v.z;
-                            wv[4 * q + 3] = v.w;
-                        }
-                    } else {
-                        // w_mode 1 copies from the 16-byte boundary below the row segment
-                        const uint32_t* rowp = stage + row * kWPitch + w_off + 8 * hh;
-#pragma unroll
-                        for (int w = 0; w < 8; ++w) wv[w] = rowp[w];
+                    for (int q = 0; q < 2; ++q) {
+                        const uint4 v = rowp[(4 * (it & 1) + 2 * hh + q) ^ (row & 7)];
+                        wv[4 * q + 0] = v.x;
+                        wv[4 * q + 1] = v.y;
+                        wv[4 * q + 2] = v.z;
+                        wv[4 * q + 3] = v.w;
                     }
                 };
                 uint32_t wa[8], wb[8];
@@ -528,66 +504,122 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
 
             // ------------------------------------------------- epilogue ----
-            // Accumulators that received at least one k-block of this item.
-            const int n_acc = n_kb < C::kIssuers ? n_kb : C::kIssuers;
+            // Every issuer accumulated at least one k-block of the segment (segments
+            // hold an even, non-zero number of k-blocks and kIssuers <= 2).
             if (!warp_wait(acc_full, n_local & 1, abort_flag)) { ok = false; break; }
             tc_fence_after();
             const int64_t n = n0 + row;
             float bias_f = 0.0f;
             if (p.bias != nullptr && n < p.N) bias_f = __bfloat162float(p.bias[n]);
+            // Final epilogue of 16 accumulator columns starting at c0.
+            auto finish = [&](int c0, const uint32_t (&acc)[16]) {
+                if (n >= p.N) return;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int m = m0 + c0 + j;
+                    if (m >= p.M) break;
+                    float yv;
+                    if constexpr (KIND == Kind::F16) {
+                        yv = __fmul_rn(__uint_as_float(acc[j]), p.scale);
+                    } else {
+                        const int acc_i = (int)acc[j] - 2 * __ldg(p.rowsum + m);
+                        if (p.acc_out) p.acc_out[(int64_t)m * p.N + n] = acc_i;
+                        const float f = __fmul_rn(p.scale, __ldg(p.s_x + m));
+                        yv = __fmul_rn((float)acc_i, f);
+                    }
+                    if (p.y != nullptr) {
+                        if (p.y_f32) {
+                            if (p.bias) yv = __fadd_rn(yv, bias_f);
+                            static_cast<float*>(p.y)[(int64_t)m * p.N + n] = yv;
+                        } else {
+                            __nv_bfloat16 t = __float2bfloat16_rn(yv);
+                            if (p.bias) t = __float2bfloat16_rn(__fadd_rn(__bfloat162float(t), bias_f));
+                            static_cast<__nv_bfloat16*>(p.y)[(int64_t)m * p.N + n] = t;
+                        }
+                    }
+                }
+            };
+            auto add_into = [&](uint32_t& d, uint32_t v) {
+                if constexpr (KIND == Kind::F16)
+                    d = __float_as_uint(__fadd_rn(__uint_as_float(d), __uint_as_float(v)));
+                else
+                    d = (uint32_t)((int)d + (int)v);
+            };
+            // Split tiles publish partials to slot 0 (the CTA's first tile) or 1.
+            const int slot = g.tile == my_first_tile ? 0 : 1;
+            uint32_t* part = p.partials + ((size_t)(blockIdx.x * 2 + slot) * kRows + row) * BT;
+            // This thread's accumulator columns: chunks c0 = 16*half + 64*i.
 #pragma unroll 1
             for (int c0 = 16 * half; c0 < BT; c0 += 16 * kUnpackGroups) {
                 if (m0 + c0 >= p.M) break;  // warp-uniform
-                uint32_t v[16];
-                tmem_ld16(tmem_base + lane_base + ((it_item % C::kIssuers) * BT) + c0, v);
+                uint32_t acc[16], v[16];
+                tmem_ld16(tmem_base + lane_base + (it_item % C::kIssuers) * BT + c0, acc);
                 tmem_wait_ld();
-                float accf[16];
-                int acci[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    accf[j] = __uint_as_float(v[j]);
-                    acci[j] = (int)v[j];
-                }
-                for (int a = 1; a < n_acc; ++a) {
-                    const int d_i = (it_item + a) % C::kIssuers;
-                    tmem_ld16(tmem_base + lane_base + d_i * BT + c0, v);
+                for (int a = 1; a < C::kIssuers; ++a) {
+                    tmem_ld16(tmem_base + lane_base + ((it_item + a) % C::kIssuers) * BT + c0, v);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        accf[j] = __fadd_rn(accf[j], __uint_as_float(v[j]));
-                        acci[j] += (int)v[j];
-                    }
+                    for (int j = 0; j < 16; ++j) add_into(acc[j], v[j]);
                 }
-                if (n < p.N) {
+                if (g.whole) {
+                    finish(c0, acc);
+                } else {
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int m = m0 + c0 + j;
-                        if (m >= p.M) break;
-                        float yv;
-                        if constexpr (KIND == Kind::F16) {
-                            yv = __fmul_rn(accf[j], p.scale);
-                        } else {
-                            const int acc_i = acci[j] - 2 * __ldg(p.rowsum + m);
-                            if (p.acc_out) p.acc_out[(int64_t)m * p.N + n] = acc_i;
-                            const float f = __fmul_rn(p.scale, __ldg(p.s_x + m));
-                            yv = __fmul_rn((float)acc_i, f);
-                        }
-                        if (p.y != nullptr) {
-                            if (p.y_f32) {
-                                if (p.bias) yv = __fadd_rn(yv, bias_f);
-                                static_cast<float*>(p.y)[(int64_t)m * p.N + n] = yv;
-                            } else {
-                                __nv_bfloat16 t = __float2bfloat16_rn(yv);
-                                if (p.bias) t = __float2bfloat16_rn(__fadd_rn(__bfloat162float(t), bias_f));
-                                static_cast<__nv_bfloat16*>(p.y)[(int64_t)m * p.N + n] = t;
-                            }
-                        }
-                    }
+                    for (int j = 0; j < 16; j += 4)
+                        *reinterpret_cast<uint4*>(part + c0 + j) = make_uint4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
                 }
             }
+            // TMEM is free for the next segment.
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty);
+
+            if (!g.whole) {
+                // Each warp owns a fixed slice of the tile (its 32 rows x its
+                // column chunks) in every contributing CTA, so arrivals are
+                // counted per (tile, warp): the last warp to publish its slice
+                // sums that slice over all contributors, in CTA order.
+                const int P = p.n_kb / 2;
+                const int c_first = owner_of(p, (int64_t)g.tile * P);
+                const int c_last = owner_of(p, (int64_t)g.tile * P + P - 1);
+                __threadfence();
+                __syncwarp();
+                int last = 0;
+                if (lane == 0) {
+                    int* ctr = p.counters + (size_t)g.tile * kUnpackWarps + warp;
+                    last = atomicAdd(ctr, 1) == c_last - c_first;
+                    if (last) *ctr = 0;  // ready for the next launch
+                }
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    __threadfence();
+#pragma unroll 1
+                    for (int c0 = 16 * half; c0 < BT; c0 += 16 * kUnpackGroups) {
+                        if (m0 + c0 >= p.M) break;
+                        uint32_t acc[16];
+                        for (int c = c_first; c <= c_last; ++c) {
+                            const int slot_c = g.tile == (int)(range_begin(p, c) / P) ? 0 : 1;
+                            const uint32_t* pc = p.partials + ((size_t)(c * 2 + slot_c) * kRows + row) * BT + c0;
+#pragma unroll
+                            for (int j = 0; j < 16; j += 4) {
+                                const uint4 q4 = __ldcg(reinterpret_cast<const uint4*>(pc + j));
+                                if (c == c_first) {
+                                    acc[j] = q4.x;
+                                    acc[j + 1] = q4.y;
+                                    acc[j + 2] = q4.z;
+                                    acc[j + 3] = q4.w;
+                                } else {
+                                    add_into(acc[j], q4.x);
+                                    add_into(acc[j + 1], q4.y);
+                                    add_into(acc[j + 2], q4.z);
+                                    add_into(acc[j + 3], q4.w);
+                                }
+                            }
+                        }
+                        finish(c0, acc);
+                    }
+                }
+            }
         }
     }
 
@@ -654,11 +686,83 @@ int device_sm_count() {
 
 static int decode_tile(int64_t M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
 
-size_t linear_workspace_bytes(int kind, int64_t M, int64_t, int64_t K) {
-    if (kind != PN_BF16 || M <= 0 || M > 64) return 0;
+// k-blocks per item: enough to cover the packed words, rounded up to even so
+// that weight stages (2 k-blocks each) never straddle items.  The padding block
+// multiplies zero activations (past K) by zero-filled weights.
+static int n_kblocks(int64_t KP) {
+    const int64_t n = (KP * kPerWord + kKB - 1) / kKB;
+    return (int)((n + 1) & ~int64_t(1));
+}
+
+static size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
+static int64_t w_pitch(int64_t KP) { return (KP + 3) & ~int64_t(3); }
+
+// Token tile for a call: the kernel instantiation launch_kind picks.
+static int token_tile(int kind, int64_t M) {
+    if (M <= 16) return 16;
+    if (M <= 32) return 32;
+    if (M <= 64) return 64;
+    if (kind == PN_BF16 || M <= 128) return 128;
+    return 256;
+}
+
+// Workspace sections, each 256-byte aligned:
+//   [decode activation slabs (bf16, M <= 64)]
+//   [weights re-pitched to 16-byte rows (K_packs % 4 != 0)]
+//   [split-tile partials: grid x 2 x 128 x BT x 4 bytes]
+//   [split-tile arrival counters: one int per tile and unpack warp]
+// Tiles split across CTAs only while there are few of them per SM; with many
+// tiles whole-tile ranges already balance to within one tile.
+struct WsLayout {
+    size_t xperm, wpitch, partials, counters, total;
+    int64_t n_items, total_pairs;
+    int grid, bt, n_kb, unit;
+};
+static WsLayout ws_layout(int kind, int64_t M, int64_t N, int64_t K, bool allow_split) {
+    WsLayout w{};
     const int64_t KP = (K + kPerWord - 1) / kPerWord;
-    const int64_t n_kb = (KP * kPerWord + kKB - 1) / kKB;
-    return (size_t)(n_kb * decode_tile(M) * 32 * 10);
+    w.bt = token_tile(kind, M);
+    w.n_kb = n_kblocks(KP);
+    w.n_items = ((N + kRows - 1) / kRows) * ((M + w.bt - 1) / w.bt);
+    w.total_pairs = w.n_items * (w.n_kb / 2);
+    int sms = device_sm_count();
+    if (sms <= 0) sms = 148;
+    const bool split = allow_split && w.n_items % sms != 0 && w.n_items < 8 * (int64_t)sms;
+    w.unit = split ? 1 : w.n_kb / 2;
+    const int64_t units = w.total_pairs / w.unit;
+    w.grid = (int)(units < sms ? units : sms);
+    size_t off = 0;
+    w.xperm = off;
+    if (kind == PN_BF16 && M >= 1 && M <= 64) off += round256((size_t)w.n_kb * w.bt * 32 * 10);
+    w.wpitch = off;
+    if (KP % 4 != 0) off += round256((size_t)N * w_pitch(KP) * 4);
+    w.partials = off;
+    w.counters = off;
+    if (split) {
+        off += round256((size_t)w.grid * 2 * kRows * w.bt * 4);
+        w.counters = off;
+        off += round256((size_t)w.n_items * kUnpackWarps * 4);
+    }
+    w.total = off;
+    return w;
+}
+size_t linear_workspace_bytes(int kind, int64_t M, int64_t N, int64_t K) {
+    if (M <= 0 || N <= 0) return 0;
+    return ws_layout(kind, M, N, K, true).total;
+}
+size_t linear_workspace_min_bytes(int kind, int64_t M, int64_t N, int64_t K) {
+    if (M <= 0 || N <= 0) return 0;
+    return ws_layout(kind, M, N, K, false).total;
+}
+
+// Copies packed rows into a 16-byte pitch so that TMA can address them.
+__global__ void __launch_bounds__(256) repitch_kernel(const int32_t* __restrict__ src, int64_t N, int64_t KP,
+                                                      int64_t pitch, int32_t* __restrict__ dst) {
+    const int64_t total = N * KP;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t n = i / KP;
+        dst[n * pitch + (i - n * KP)] = __ldg(src + i);
+    }
 }
 
 template <Kind KIND, int BT>
@@ -703,19 +807,43 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
             return PN_ERR_ALIGN;
         }
     }
-    // Packed weights: one TMA box per k-block when rows are 16-byte aligned.
+    // Packed weights: one 128-byte-swizzled TMA box per weight stage (128 rows
+    // x 32 words).  TMA needs 16-byte row pitches; other shapes are first copied
+    // into the workspace with the pitch rounded up.
+    // The full layout when the workspace holds it, else whole tiles per CTA.
+    WsLayout L = ws_layout(a.kind, a.M, a.N, a.K, true);
+    if (a.workspace_bytes < L.total) L = ws_layout(a.kind, a.M, a.N, a.K, false);
+    if (L.bt != BT) {
+        *why = "internal: token tile mismatch";
+        return PN_ERR_ARG;
+    }
+    if ((L.total > 0 && a.workspace == nullptr) || a.workspace_bytes < L.total ||
+        reinterpret_cast<uintptr_t>(a.workspace) % 256) {
+        *why = "workspace missing, too small or not 256-byte aligned";
+        return PN_ERR_WORKSPACE;
+    }
+    uint8_t* ws = static_cast<uint8_t*>(a.workspace);
+    const bool repitch = a.KP % 4 != 0;
+    const int64_t pitch = repitch ? w_pitch(a.KP) : a.KP;
+    const int32_t* wsrc = a.packed;
+    if (repitch) {
+        int32_t* dst = reinterpret_cast<int32_t*>(ws + L.wpitch);
+        const int64_t total = a.N * a.KP;
+        const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+        repitch_kernel<<<blocks, 256, 0, s>>>(a.packed, a.N, a.KP, pitch, dst);
+        wsrc = dst;
+    }
     CUtensorMap wmap;
-    std::memset(&wmap, 0, sizeof(wmap));
-    const bool base16 = reinterpret_cast<uintptr_t>(a.packed) % 16 == 0;
-    int w_mode = base16 ? 1 : 2;
-    if (base16 && a.KP % 4 == 0) {
+    {
         cuuint64_t dims[2] = {(cuuint64_t)a.KP, (cuuint64_t)a.N};
-        cuuint64_t strides[1] = {(cuuint64_t)(a.KP * 4)};
-        cuuint32_t box[2] = {(cuuint32_t)kWordsPerKB, (cuuint32_t)kRows};
-        if (encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, const_cast<int32_t*>(a.packed), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
-            w_mode = 0;
+        cuuint64_t strides[1] = {(cuuint64_t)(pitch * 4)};
+        cuuint32_t box[2] = {(cuuint32_t)kWStageWords, (cuuint32_t)kRows};
+        if (encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, const_cast<int32_t*>(wsrc), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+            *why = "cuTensorMapEncodeTiled rejected the packed-weight layout";
+            return PN_ERR_ALIGN;
+        }
     }
     DqmmParams prm;
     prm.packed = a.packed;
@@ -725,22 +853,20 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     prm.n_row_tiles = (int)((a.N + kRows - 1) / kRows);
     const int n_tok_tiles = (int)((a.M + BT - 1) / BT);
     prm.n_items = prm.n_row_tiles * n_tok_tiles;
-    // k-blocks covering the packed words (activation slabs past K are zero-filled)
-    prm.n_kb = (int)((a.KP * kPerWord + kKB - 1) / kKB);
-    prm.w_mode = w_mode;
+    prm.total_pairs = L.total_pairs;
+    prm.unit = L.unit;
+    prm.partials = reinterpret_cast<uint32_t*>(ws + L.partials);
+    prm.counters = reinterpret_cast<int*>(ws + L.counters);
+    prm.n_kb = n_kblocks(a.KP);
+    prm.w_pad = repitch;
     prm.x_mode = x_mode;
     prm.packed_bytes = a.N * a.KP * 4;
-    prm.xperm = static_cast<const uint8_t*>(a.workspace);
+    prm.xperm = ws + L.xperm;
     if (C::kPerm) {
-        const size_t need = linear_workspace_bytes(PN_BF16, a.M, a.N, a.K);
-        if (a.workspace == nullptr || a.workspace_bytes < need || reinterpret_cast<uintptr_t>(a.workspace) % 16) {
-            *why = "workspace missing, too small or not 16-byte aligned";
-            return PN_ERR_WORKSPACE;
-        }
         const int64_t total = a.M * (int64_t)prm.n_kb * kKB;
         const int blocks = (int)((total + 255) / 256 < 1024 ? (total + 255) / 256 : 1024);
         permute_x_kernel<BT><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(a.x), (int)a.M, a.K, prm.n_kb,
-                                                    static_cast<uint8_t*>(a.workspace));
+                                                    ws + L.xperm);
     }
     prm.scale = a.scale;
     prm.bias = static_cast<const __nv_bfloat16*>(a.bias);
@@ -763,9 +889,15 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
         }
         if (dev >= 0 && dev < 64) attr_done[dev] = true;
     }
-    int sms = device_sm_count();
-    if (sms <= 0) sms = 148;
-    const int grid = prm.n_items < sms ? prm.n_items : sms;
+    const int grid = L.grid;
+    if (L.unit == 1) {
+        cudaError_t e = cudaMemsetAsync(prm.counters, 0, sizeof(int) * kUnpackWarps * (size_t)prm.n_items, s);
+        if (e != cudaSuccess) {
+            *err = e;
+            *why = "cudaMemsetAsync of the split-tile counters";
+            return PN_ERR_CUDA;
+        }
+    }
     kern<<<grid, kThreads, C::kSmem, s>>>(xmap, wmap, prm);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {

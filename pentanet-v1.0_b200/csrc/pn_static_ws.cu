@@ -11,12 +11,15 @@
 // process exits, and no call allocates or frees anything.
 //
 // Limits and sharing:
-//   * the scratch a call needs must be <= kStaticScratchBytes (4 MiB: e.g.
-//     K = 28672 at up to 64 tokens); larger requests are rejected with
-//     PN_ERR_WORKSPACE before anything is enqueued;
+//   * the least scratch a call runs with must be <= kStaticScratchBytes
+//     (4 MiB: e.g. K = 28672 at up to 64 tokens); larger requests are rejected
+//     with PN_ERR_WORKSPACE before anything is enqueued.  When the array also
+//     holds the split-tile partial sums the kernel uses them, else it gives
+//     each SM whole tiles;
 //   * all calls on a device share the one array and it keeps the last call's
-//     contents.  The decode kernel writes every byte it later reads, so nothing
-//     needs clearing between calls -- but calls that can overlap on the GPU
+//     contents.  Each call sets every byte it later reads (the split-tile
+//     counters by a memset on its stream), so nothing needs clearing between
+//     calls -- but calls that can overlap on the GPU
 //     (different streams without ordering between them) race on the array and
 //     must be serialised by the caller;
 //   * the first call on a device looks up the array's device address
@@ -64,7 +67,7 @@ int static_scratch(void** out, const char** why) {
 extern "C" int pn_linear_bf16_nows(const void* x, int64_t M, int64_t K, const int32_t* packed, int64_t N,
                                    int64_t K_packs, float scale, const void* bias, void* y, int y_dtype,
                                    void* stream) {
-    const size_t need = pn::linear_workspace_bytes(PN_BF16, M, N, K);
+    const size_t need = pn::linear_workspace_min_bytes(PN_BF16, M, N, K);
     if (need > pn::kStaticScratchBytes)
         return fail(PN_ERR_WORKSPACE,
                     "pn_linear_bf16_nows: this shape needs %zu bytes of scratch; the static array holds %zu "

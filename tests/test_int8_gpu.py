@@ -91,3 +91,24 @@ def test_cfg3_full_size(cuda_device, K, N):
     want_c = orc.matmul_i8(xq[:, :K].cpu().numpy(), w8[cols].cpu().numpy())
     assert np.array_equal(acc[:, cols].cpu().numpy(), want_c)
     assert np.array_equal(y[rows].cpu().numpy(), orc.dequant_i8(want, s_x[rows].cpu().numpy(), gamma))
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 384, 28672), (100, 1000, 3072), (300, 640, 1600)])
+def test_int8_split_and_whole_tile_schedules(cuda_device, M, N, K):
+    """The recommended workspace (split K ranges, partial sums) and the minimum
+    one (whole tiles per SM) give the same exact int32 accumulators."""
+    import ctypes
+    import penta_native as nat
+    L = nat.load()
+    packed, _, gamma = pk.quantize_and_pack(gen_weight(N, K, seed=M + N + K).to(cuda_device))
+    x = gen_act(M, K, seed=K + 1).to(torch.bfloat16)
+    xq, s_x, rowsum = pk.quantize_activations_i8(x.to(cuda_device))
+    want = orc.matmul_i8(orc.quant_act_i8(x.float().numpy())[0], orc.unpack(packed.cpu().numpy(), K))
+    for nbytes in (L.pn_linear_workspace_size(nat.PN_I8, M, N, K), L.pn_linear_workspace_min_size(nat.PN_I8, M, N, K)):
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=cuda_device)
+        acc = torch.empty(M, N, dtype=torch.int32, device=cuda_device)
+        st = L.pn_linear_i8(xq.data_ptr(), xq.shape[1], s_x.data_ptr(), rowsum.data_ptr(), M, K, packed.data_ptr(),
+                            N, packed.shape[1], ctypes.c_float(gamma), None, None, nat.PN_F32, acc.data_ptr(),
+                            ws.data_ptr(), nbytes, nat.stream_of(xq))
+        assert st == nat.PN_OK, L.pn_last_error()
+        assert np.array_equal(acc.cpu().numpy(), want), f"workspace {nbytes}"

@@ -165,3 +165,44 @@ def test_repeat_calls_bit_identical(cuda_device, M, N, K):
     xf = x.float().cpu().numpy()
     rows = [0, N // 2, N - 1]
     assert_close(first[:, rows].cpu().numpy(), orc.matmul_f64(xf, w8[rows], gamma), what="repeat")
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 384, 28672), (7, 8192, 3072), (64, 200, 8192), (200, 300, 1536),
+                                   (33, 1000, 1001)])
+def test_split_and_whole_tile_schedules(cuda_device, M, N, K):
+    """With the recommended workspace the kernel splits tiles' K ranges over
+    SMs (partial sums reduced by the last arriving CTA); with the minimum it
+    gives each SM whole tiles.  Both must match the oracle and be repeatable."""
+    import ctypes
+    import penta_native as nat
+    L = nat.load()
+    packed, gamma, w8 = _layer(N, K, seed=N + 3 * K, dev=cuda_device)
+    x = gen_act(M, K, seed=M + 7).to(torch.bfloat16).to(cuda_device)
+    KP = packed.shape[1]
+    full = L.pn_linear_workspace_size(nat.PN_BF16, M, N, K)
+    least = L.pn_linear_workspace_min_size(nat.PN_BF16, M, N, K)
+    assert 0 <= least <= full
+    want = orc.matmul_f64(x.float().cpu().numpy(), w8, gamma)
+    outs = []
+    for nbytes in (full, least):
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=cuda_device)
+        runs = []
+        for _ in range(3):
+            y = torch.empty(M, N, dtype=torch.float32, device=cuda_device)
+            st = L.pn_linear_bf16(x.data_ptr(), M, K, packed.data_ptr(), N, KP, ctypes.c_float(gamma), None,
+                                  y.data_ptr(), nat.PN_F32, ws.data_ptr(), nbytes, nat.stream_of(x))
+            assert st == nat.PN_OK, L.pn_last_error()
+            runs.append(y)
+        torch.cuda.synchronize()
+        assert all(torch.equal(r, runs[0]) for r in runs[1:]), f"workspace {nbytes}: repeat calls differ"
+        assert_close(runs[0].cpu().numpy(), want, what=f"M={M} N={N} K={K} workspace {nbytes}")
+        outs.append(runs[0])
+    if least < full:
+        # one byte short of the minimum is refused
+        ws = torch.empty(max(least, 1), dtype=torch.uint8, device=cuda_device)
+        y = torch.empty(M, N, dtype=torch.float32, device=cuda_device)
+        if least > 0:
+            st = L.pn_linear_bf16(x.data_ptr(), M, K, packed.data_ptr(), N, KP, ctypes.c_float(gamma), None,
+                                  y.data_ptr(), nat.PN_F32, ws.data_ptr(), least - 1, nat.stream_of(x))
+            assert st == nat.PN_ERR_WORKSPACE
+    assert nat.device_status(reset=True) == 0
