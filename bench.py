@@ -220,24 +220,30 @@ def run_reference(args):
 # ------------------------------------------------------------ our arm -----
 
 def run_profile_case(args):
-    """Small case for ncu --set full: the 8192->28672 layer (94 MB packed, one
-    copy), one launch each at M = 1, 8, 64, after three warm-up launches."""
+    """Small case for ncu --set full: both 70B-class layers (94 MB packed each,
+    one copy), one launch each at M = 1, 8, 64, after three warm-up launches."""
     import torch
     import penta_kernel as pk
     dev = torch.device("cuda", 0)
     gen = torch.Generator(device=dev).manual_seed(1234)
-    K, N = SHAPES[0]
-    w = torch.randn(N, K, device=dev, generator=gen) * 0.02
-    packed, _, s = pk.quantize_and_pack(w)
-    del w
+    layers = []
+    for (K, N) in SHAPES:
+        w = torch.randn(N, K, device=dev, generator=gen) * 0.02
+        packed, _, s = pk.quantize_and_pack(w)
+        del w
+        layers.append((K, N, packed, s))
     torch.cuda.empty_cache()
-    xs = {M: torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16) for M in BATCHES}
+    xs = {(M, K): torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16)
+          for M in BATCHES for (K, _, _, _) in layers}
+    K0, _, p0, s0 = layers[0]
     for _ in range(3):
-        pk.penta_linear(xs[1], packed, s, K)
-    for M in BATCHES:
-        pk.penta_linear(xs[M], packed, s, K)
+        pk.penta_linear(xs[(1, K0)], p0, s0, K0)
+    for (K, N, packed, s) in layers:
+        for M in BATCHES:
+            pk.penta_linear(xs[(M, K)], packed, s, K)
     torch.cuda.synchronize()
-    print(json.dumps({"profile_case": "dqmm 8192->28672", "launches": 3 + len(BATCHES)}))
+    print(json.dumps({"profile_case": "dqmm 8192->28672 and 28672->8192", "warmup_launches": 3,
+                      "launches": len(layers) * len(BATCHES)}))
 
 
 def run_ours(args):
