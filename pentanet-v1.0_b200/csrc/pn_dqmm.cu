@@ -42,7 +42,7 @@ constexpr int kLoadWarp = kUnpackWarps;       // weight staging, even stages
 constexpr int kLoadWarp2 = kUnpackWarps + 1;  // weight staging, odd stages
 constexpr int kXLoadWarp = kUnpackWarps + 2;  // activation staging
 constexpr int kMmaWarp = kUnpackWarps + 3;    // TMEM allocation + MMA issue; warps kMmaWarp.. issue MMAs
-constexpr int kMaxIssuers = 2;
+constexpr int kMaxIssuers = 4;
 constexpr int kThreads = 32 * (kUnpackWarps + 3 + kMaxIssuers);
 constexpr int kTmemCols = 512;
 
@@ -56,6 +56,7 @@ struct KindT<Kind::F16> {
     static constexpr int kSlabElems = 16;  // elements per 32-byte slab = MMA K
     static constexpr int kSteps = 10;      // MMAs per k-block
     static constexpr int kACols = 80;      // TMEM columns of A per k-block (2 bf16 per column)
+    static constexpr int kAPerKB = 2;      // TMEM operand stages per k-block (8 words / 5 MMAs each)
 };
 template <>
 struct KindT<Kind::I8> {
@@ -63,21 +64,22 @@ struct KindT<Kind::I8> {
     static constexpr int kSlabElems = 32;
     static constexpr int kSteps = 5;
     static constexpr int kACols = 40;      // 4 codes per column
+    static constexpr int kAPerKB = 1;
 };
 
 template <Kind KIND, int BT>
 struct Cfg {
     using T = KindT<KIND>;
-    // Small token tiles (decode): activations are staged with cp.async (only the
-    // real token rows, 16 bytes per copy) and several warps issue MMAs, each
-    // into its own accumulator -- one thread can issue an MMA only every ~50
-    // cycles, which small-N MMAs cannot hide.  Large tiles (prefill): TMA boxes
-    // and one issuer.
+    // Small token tiles (decode) run several MMA-issuing warps, each taking
+    // every kIssuers-th k-block into its own accumulator: one warp issues an
+    // MMA only every ~40-80 cycles, which the short MMAs of a 16- or 32-token
+    // tile (8-16 tensor cycles) cannot hide.  A 64-token MMA takes ~32 tensor
+    // cycles, so two issuers keep the tensor pipe busy; large tiles use one.
     static constexpr bool kXTma = BT >= 128;
     // bf16 decode tiles use the permuted unpack; their activations come
     // pre-arranged (permute_x_kernel) and are staged with one bulk copy per k-block.
     static constexpr bool kPerm = KIND == Kind::F16 && BT <= 64;
-    static constexpr int kIssuers = BT <= 64 ? 2 : 1;
+    static constexpr int kIssuers = BT <= 32 ? 4 : (BT <= 64 ? 2 : 1);
     static constexpr int kSlabBytes = BT * 32;
     static constexpr int kXStageBytes = kSlabBytes * T::kSteps;
     static constexpr int kChunksPerRow = kKB * T::kXElem / 16;      // 16-byte pieces of one row per k-block
@@ -88,8 +90,13 @@ struct Cfg {
     // activation rings) must each see every phase of the slots they use, in
     // order; otherwise a parity wait can pass on a phase two rounds old.  So
     // each ring depth is a multiple of the number of parties taking turns on it.
-    static constexpr int kSAfit = (kTmemCols - kA0) / T::kACols;
-    static constexpr int kSA = (kSAfit >= 8 ? 8 : kSAfit) / kUnpackGroups * kUnpackGroups;
+    // TMEM operand stages: 40 columns each (half a bf16 k-block, a whole int8
+    // one), so that an unpack group fills one stage while the MMAs read its other.
+    static constexpr int kAStageCols = T::kACols / T::kAPerKB;
+    static constexpr int kStepsPerA = T::kSteps / T::kAPerKB;
+    static constexpr int kAParties = kUnpackGroups * T::kAPerKB;  // stage uses per round of groups
+    static constexpr int kSAfit = (kTmemCols - kA0) / kAStageCols;
+    static constexpr int kSA = (kSAfit >= 8 ? 8 : kSAfit) / kAParties * kAParties;
     static constexpr int kBudget = 200 * 1024;
     static constexpr int kSW = kXStageBytes >= 40 * 1024 ? 4 : (kXStageBytes >= 20 * 1024 ? 6 : 8);
     static constexpr int kSXfit = (kBudget - kSW * kWStageBytes) / kXStageBytes;
@@ -98,10 +105,10 @@ struct Cfg {
     static constexpr int kNumBars = 2 * kSW + 2 * kSX + 2 * kSA + 3 + kIssuers;
     static constexpr int kSmem = kBarOff + kNumBars * 8 + 16 + 1024;  // + tmem slot, abort and last-arriver flags + align slack
     static_assert(kSX >= 2 && kSX % kIssuers == 0, "activation ring");
-    static_assert(kSA >= kUnpackGroups && kSA % kUnpackGroups == 0 && kSA % kIssuers == 0, "TMEM operand ring");
+    static_assert(kSA >= kAParties && kSA % kAParties == 0 && kSA % (kIssuers * T::kAPerKB) == 0, "TMEM operand ring");
     static_assert(kSW % 2 == 0, "weight ring: two producers, two k-blocks per stage");
     static_assert((kSX * kXStageBytes) % 1024 == 0, "weight stages must stay 1024-byte aligned (128B swizzle)");
-    static_assert(kA0 + kSA * T::kACols <= kTmemCols, "TMEM over-subscribed");
+    static_assert(kA0 + kSA * kAStageCols <= kTmemCols, "TMEM over-subscribed");
     static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "token tile");
 };
 
@@ -127,12 +134,29 @@ struct DqmmParams {
     const int32_t* rowsum;
 };
 
+// (a & M) | C as one LOP3.  Written out because the compiler otherwise emits
+// an AND and an OR when both M and C are immediates, which costs the unpack
+// loops a third of their integer-pipe throughput.
+template <uint32_t M, uint32_t C>
+__device__ __forceinline__ uint32_t and_or(uint32_t a) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "n"(M), "n"(C));
+    return r;
+}
+// (a & M) | c for a register c.
+template <uint32_t M>
+__device__ __forceinline__ uint32_t and_or_r(uint32_t a, uint32_t c) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "n"(M), "r"(c));
+    return r;
+}
+
 // bf16 weights of one packed word: five bf16x2 registers, natural k order
 // (register j holds k = 2j in the low half and k = 2j+1 in the high half).
 // (128 + c) is built in the mantissa of a bf16 with exponent 2^7, then 130 is
 // subtracted: exact c - 2 for every code.
 __device__ __forceinline__ uint32_t bf16_pair(uint32_t lo_src, uint32_t hi_src) {
-    uint32_t t = (lo_src & 0x00000007u) | (hi_src & 0x00070000u) | 0x43004300u;
+    const uint32_t t = and_or_r<0x00070000u>(hi_src, and_or<0x00000007u, 0x43004300u>(lo_src));
     uint32_t r;
     asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(t), "r"(0x43024302u));
     return r;
@@ -167,11 +191,11 @@ __device__ __forceinline__ void unpack_word_bf16_perm(uint32_t p, uint32_t* r) {
     const uint32_t r2 = p >> 2;
     const uint32_t r8 = p >> 8;
     // (code j at bit o_lo, code j+5 at bit 16+o_hi) | bf16 128.0 in both halves
-    r[0] = bf16_sub2((l1 & 0x0007000Eu) | 0x43004300u, 0x43024304u);  // 132 lo, 130 hi
-    r[1] = bf16_sub2((r2 & 0x0007000Eu) | 0x43004300u, 0x43024304u);
-    r[2] = bf16_sub2((r2 & 0x00380070u) | 0x43004300u, 0x43104320u);  // 160 lo, 144 hi
-    r[3] = bf16_sub2((r8 & 0x0007000Eu) | 0x43004300u, 0x43024304u);
-    r[4] = bf16_sub2((r8 & 0x00380070u) | 0x43004300u, 0x43104320u);
+    r[0] = bf16_sub2(and_or<0x0007000Eu, 0x43004300u>(l1), 0x43024304u);  // 132 lo, 130 hi
+    r[1] = bf16_sub2(and_or<0x0007000Eu, 0x43004300u>(r2), 0x43024304u);
+    r[2] = bf16_sub2(and_or<0x00380070u, 0x43004300u>(r2), 0x43104320u);  // 160 lo, 144 hi
+    r[3] = bf16_sub2(and_or<0x0007000Eu, 0x43004300u>(r8), 0x43024304u);
+    r[4] = bf16_sub2(and_or<0x00380070u, 0x43004300u>(r8), 0x43104320u);
 }
 
 // Unsigned codes of two packed words (20 weights) as five int8x4 registers in
@@ -180,7 +204,7 @@ __device__ __forceinline__ void unpack_word_bf16_perm(uint32_t p, uint32_t* r) {
 __device__ __forceinline__ uint32_t spread4(uint32_t t) {
     const uint32_t e = t & 0x1C7u;  // codes 0 and 2
     const uint32_t o = t & 0xE38u;  // codes 1 and 3
-    return ((e * 0x401u) & 0x00070007u) | ((o * 0x8020u) & 0x07000700u);
+    return and_or_r<0x00070007u>(e * 0x401u, (o * 0x8020u) & 0x07000700u);
 }
 __device__ __forceinline__ void unpack_pair_u8(uint32_t p0, uint32_t p1, uint32_t* r) {
     const uint32_t lo = p0 | (p1 << 30);
@@ -358,10 +382,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= kMmaWarp) {
         // --------------------------------------------------------- MMAs ----
-        // Issuer i (warp kMmaWarp + i, lane 0) takes the k-blocks with
-        // global index it % kIssuers == i and accumulates into D_i.
+        // Issuer i (warp kMmaWarp + i, converged; one elected lane issues)
+        // takes the k-blocks with global index it % kIssuers == i and
+        // accumulates into D_i.
         const int issuer = warp - kMmaWarp;
-        if (issuer < C::kIssuers && lane == 0) {
+        if (issuer < C::kIssuers) {
             uint32_t idesc;
             if constexpr (KIND == Kind::F16)
                 idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BT >> 3) << 17) | ((128u >> 4) << 24);
@@ -374,40 +399,48 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int64_t u = range_begin(p, blockIdx.x); u < u_end && ok; ++n_local) {
                 const Seg g = segment_at(p, u, u_end);
                 u += (g.kb1 - g.kb0) / 2;
-                if (!mbar_wait(acc_empty, (n_local & 1) ^ 1, abort_flag)) break;
+                if (!warp_wait(acc_empty, (n_local & 1) ^ 1, abort_flag)) break;
                 tc_fence_after();
                 bool first = true;
                 for (int kb = g.kb0; kb < g.kb1; ++kb, ++it) {
                     if ((int)(it % C::kIssuers) != issuer) continue;
                     const int sx = it % C::kSX;
-                    const int sa = it % C::kSA;
-                    if (!mbar_wait(&full_x[sx], (it / C::kSX) & 1, abort_flag)) { ok = false; break; }
-                    if (!mbar_wait(&full_a[sa], (it / C::kSA) & 1, abort_flag)) { ok = false; break; }
-                    tc_fence_after();
+                    if (!warp_wait(&full_x[sx], (it / C::kSX) & 1, abort_flag)) { ok = false; break; }
                     const uint8_t* xs = smem_x + sx * C::kXStageBytes;
-                    const uint32_t a_col = tmem_base + C::kA0 + sa * T::kACols;
 #pragma unroll
-                    for (int j = 0; j < T::kSteps; ++j) {
-                        const uint64_t bdesc = smem_desc_sw32(xs + j * C::kSlabBytes);
-                        const uint32_t acc = (first && j == 0) ? 0u : 1u;
-                        if constexpr (KIND == Kind::F16)
-                            mma_f16_ts(d_tmem, a_col + j * 8, bdesc, idesc, acc);
-                        else
-                            mma_i8_ts(d_tmem, a_col + j * 8, bdesc, idesc, acc);
+                    for (int hh = 0; hh < T::kAPerKB; ++hh) {
+                        const uint32_t ua = it * T::kAPerKB + hh;  // operand stage use
+                        const int sa = ua % C::kSA;
+                        if (!warp_wait(&full_a[sa], (ua / C::kSA) & 1, abort_flag)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint32_t a_col = tmem_base + C::kA0 + sa * C::kAStageCols;
+#pragma unroll
+                        for (int j = 0; j < C::kStepsPerA; ++j) {
+                            const uint64_t bdesc = smem_desc_sw32(xs + (hh * C::kStepsPerA + j) * C::kSlabBytes);
+                            const uint32_t acc = (first && j == 0) ? 0u : 1u;
+                            if constexpr (KIND == Kind::F16)
+                                mma_f16_ts_warp(d_tmem, a_col + j * 8, bdesc, idesc, acc);
+                            else
+                                mma_i8_ts_warp(d_tmem, a_col + j * 8, bdesc, idesc, acc);
+                        }
+                        first = false;
+                        tc_commit_warp(&empty_a[sa]);
                     }
-                    first = false;
-                    tc_commit(&empty_x[sx]);
-                    tc_commit(&empty_a[sa]);
+                    if (!ok) break;
+                    tc_commit_warp(&empty_x[sx]);
                 }
                 if (!ok) break;
-                if (first)
-                    mbar_arrive(acc_full);  // no k-block of this item: D_i unused
-                else
-                    tc_commit(acc_full);
+                if (first) {
+                    // no k-block of this segment: D_i unused (the epilogue skips it)
+                    if (lane == 0) mbar_arrive(acc_full);
+                    __syncwarp();
+                } else {
+                    tc_commit_warp(acc_full);
+                }
             }
-            // Every MMA this thread issued completes before tensor memory is freed.
-            tc_commit(&drain[issuer]);
-            mbar_wait_drain(&drain[issuer], 0);
+            // Every MMA this warp issued completes before tensor memory is freed.
+            tc_commit_warp(&drain[issuer]);
+            if (lane == 0) mbar_wait_drain(&drain[issuer], 0);
         }
         __syncwarp();
     } else {
@@ -455,15 +488,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty_w[sw]);
 
-                const int sa = it % C::kSA;
-                if (!warp_wait(&empty_a[sa], ((it / C::kSA) & 1) ^ 1, abort_flag)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t a_addr = tmem_base + lane_base + C::kA0 + sa * T::kACols;
-                if constexpr (KIND == Kind::F16) {
-                    // 16 words -> 80 columns, in two halves of 8 words / 40 columns
 #pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {
-                        uint32_t cols[40];
+                for (int hh = 0; hh < T::kAPerKB; ++hh) {
+                    const uint32_t ua = it * T::kAPerKB + hh;  // operand stage use
+                    const int sa = ua % C::kSA;
+                    if (!warp_wait(&empty_a[sa], ((ua / C::kSA) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_addr = tmem_base + lane_base + C::kA0 + sa * C::kAStageCols;
+                    uint32_t cols[40];
+                    if constexpr (KIND == Kind::F16) {
+                        // 8 words (half the k-block) -> 40 columns
 #pragma unroll
                         for (int w = 0; w < 8; ++w) {
                             const uint32_t word = hh ? wb[w] : wa[w];
@@ -472,21 +506,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                             else
                                 unpack_word_bf16(word, &cols[5 * w]);
                         }
+                    } else {
+                        // 8 word pairs -> 40 columns
 #pragma unroll
-                        for (int c = 0; c < 5; ++c) {
-                            uint32_t v8[8];
-#pragma unroll
-                            for (int i = 0; i < 8; ++i) v8[i] = cols[8 * c + i];
-                            tmem_st8(a_addr + 40 * hh + 8 * c, v8);
+                        for (int w = 0; w < 4; ++w) {
+                            unpack_pair_u8(wa[2 * w], wa[2 * w + 1], &cols[5 * w]);
+                            unpack_pair_u8(wb[2 * w], wb[2 * w + 1], &cols[20 + 5 * w]);
                         }
-                    }
-                } else {
-                    // 8 word pairs -> 40 columns
-                    uint32_t cols[40];
-#pragma unroll
-                    for (int w = 0; w < 4; ++w) {
-                        unpack_pair_u8(wa[2 * w], wa[2 * w + 1], &cols[5 * w]);
-                        unpack_pair_u8(wb[2 * w], wb[2 * w + 1], &cols[20 + 5 * w]);
                     }
 #pragma unroll
                     for (int c = 0; c < 5; ++c) {
@@ -495,17 +521,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int i = 0; i < 8; ++i) v8[i] = cols[8 * c + i];
                         tmem_st8(a_addr + 8 * c, v8);
                     }
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&full_a[sa]);
                 }
-                tmem_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&full_a[sa]);
+                if (!ok) break;
             }
             if (!ok) break;
 
             // ------------------------------------------------- epilogue ----
-            // Every issuer accumulated at least one k-block of the segment (segments
-            // hold an even, non-zero number of k-blocks and kIssuers <= 2).
+            // Issuer (it_item + a) % kIssuers accumulated k-blocks of this segment
+            // iff a < its k-block count (segments are at least 2 k-blocks long).
             if (!warp_wait(acc_full, n_local & 1, abort_flag)) { ok = false; break; }
             tc_fence_after();
             const int64_t n = n0 + row;
@@ -555,7 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t acc[16], v[16];
                 tmem_ld16(tmem_base + lane_base + (it_item % C::kIssuers) * BT + c0, acc);
                 tmem_wait_ld();
-                for (int a = 1; a < C::kIssuers; ++a) {
+                for (int a = 1; a < C::kIssuers && a < g.kb1 - g.kb0; ++a) {
                     tmem_ld16(tmem_base + lane_base + ((it_item + a) % C::kIssuers) * BT + c0, v);
                     tmem_wait_ld();
 #pragma unroll
