@@ -402,14 +402,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!warp_wait(acc_empty, (n_local & 1) ^ 1, abort_flag)) break;
                 tc_fence_after();
                 bool first = true;
-                for (int kb = g.kb0; kb < g.kb1; ++kb, ++it) {
-                    if ((int)(it % C::kIssuers) != issuer) continue;
-                    const int sx = it % C::kSX;
-                    if (!warp_wait(&full_x[sx], (it / C::kSX) & 1, abort_flag)) { ok = false; break; }
+                // this issuer's k-blocks of the segment: global index == issuer (mod kIssuers)
+                const uint32_t it0 = it;
+                const int nkb = g.kb1 - g.kb0;
+                for (int j = (int)((issuer - it0) & (C::kIssuers - 1)); j < nkb; j += C::kIssuers) {
+                    const uint32_t ik = it0 + j;
+                    const int sx = ik % C::kSX;
+                    if (!warp_wait(&full_x[sx], (ik / C::kSX) & 1, abort_flag)) { ok = false; break; }
                     const uint8_t* xs = smem_x + sx * C::kXStageBytes;
 #pragma unroll
                     for (int hh = 0; hh < T::kAPerKB; ++hh) {
-                        const uint32_t ua = it * T::kAPerKB + hh;  // operand stage use
+                        const uint32_t ua = ik * T::kAPerKB + hh;  // operand stage use
                         const int sa = ua % C::kSA;
                         if (!warp_wait(&full_a[sa], (ua / C::kSA) & 1, abort_flag)) { ok = false; break; }
                         tc_fence_after();
@@ -429,6 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!ok) break;
                     tc_commit_warp(&empty_x[sx]);
                 }
+                it = it0 + nkb;
                 if (!ok) break;
                 if (first) {
                     // no k-block of this segment: D_i unused (the epilogue skips it)
@@ -463,11 +467,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int64_t n0 = (int64_t)(g.tile % p.n_row_tiles) * kRows;
             const int m0 = (g.tile / p.n_row_tiles) * BT;
             const uint32_t it_item = it;
-            for (int kb = g.kb0; kb < g.kb1; ++kb, ++it) {
-                if ((int)(it % kUnpackGroups) != half) continue;
-                // Weight stages hold 2 k-blocks: global k-block `it` is half (it & 1)
-                // of global stage it / 2 (every item has an even k-block count).
-                const uint32_t wst = it >> 1;
+            // this group's k-blocks of the segment: global index == half (mod 4)
+            const int nkb = g.kb1 - g.kb0;
+            for (int j = (int)((half - it_item) & (kUnpackGroups - 1)); j < nkb; j += kUnpackGroups) {
+                const uint32_t ik = it_item + j;
+                // Weight stages hold 2 k-blocks: global k-block `ik` is half (ik & 1)
+                // of global stage ik / 2 (every item has an even k-block count).
+                const uint32_t wst = ik >> 1;
                 const int sw = wst % C::kSW;
                 if (!warp_wait(&full_w[sw], (wst / C::kSW) & 1, abort_flag)) { ok = false; break; }
                 // 128-byte swizzle: 16-byte chunk q of row r sits at chunk q ^ (r & 7).
@@ -475,22 +481,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 auto load8 = [&](int hh, uint32_t (&wv)[8]) {
 #pragma unroll
                     for (int q = 0; q < 2; ++q) {
-                        const uint4 v = rowp[(4 * (it & 1) + 2 * hh + q) ^ (row & 7)];
+                        const uint4 v = rowp[(4 * (ik & 1) + 2 * hh + q) ^ (row & 7)];
                         wv[4 * q + 0] = v.x;
                         wv[4 * q + 1] = v.y;
                         wv[4 * q + 2] = v.z;
                         wv[4 * q + 3] = v.w;
                     }
                 };
-                uint32_t wa[8], wb[8];
-                load8(0, wa);
-                load8(1, wb);
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty_w[sw]);
-
 #pragma unroll
                 for (int hh = 0; hh < T::kAPerKB; ++hh) {
-                    const uint32_t ua = it * T::kAPerKB + hh;  // operand stage use
+                    // Words are read from shared memory only when needed (8 per bf16
+                    // half, all 16 for int8), which keeps register pressure down; the
+                    // weight stage is released after the last read.
+                    uint32_t wa[8], wb[8];
+                    if constexpr (KIND == Kind::F16) {
+                        load8(hh, wa);
+                    } else {
+                        load8(0, wa);
+                        load8(1, wb);
+                    }
+                    const uint32_t ua = ik * T::kAPerKB + hh;  // operand stage use
                     const int sa = ua % C::kSA;
                     if (!warp_wait(&empty_a[sa], ((ua / C::kSA) & 1) ^ 1, abort_flag)) { ok = false; break; }
                     tc_fence_after();
@@ -500,11 +510,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         // 8 words (half the k-block) -> 40 columns
 #pragma unroll
                         for (int w = 0; w < 8; ++w) {
-                            const uint32_t word = hh ? wb[w] : wa[w];
                             if constexpr (C::kPerm)
-                                unpack_word_bf16_perm(word, &cols[5 * w]);
+                                unpack_word_bf16_perm(wa[w], &cols[5 * w]);
                             else
-                                unpack_word_bf16(word, &cols[5 * w]);
+                                unpack_word_bf16(wa[w], &cols[5 * w]);
                         }
                     } else {
                         // 8 word pairs -> 40 columns
@@ -524,10 +533,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&full_a[sa]);
+                    if (lane == 0) {
+                        mbar_arrive(&full_a[sa]);
+                        if (hh == T::kAPerKB - 1) mbar_arrive(&empty_w[sw]);
+                    }
                 }
                 if (!ok) break;
             }
+            it = it_item + nkb;
             if (!ok) break;
 
             // ------------------------------------------------- epilogue ----
