@@ -48,6 +48,10 @@ COPIES = 4                                  # weight copies per shape, rotated (
 FALLBACK_HBM_GBS = 6650.0
 
 
+PREFILL_SHAPES = [(4096, 4096), (4096, 11008), (11008, 4096)]   # (K, N), 7B-class layers
+PREFILL_M = 4096
+
+
 def k_packs(K: int) -> int:
     return (K + 9) // 10
 
@@ -246,6 +250,61 @@ def run_profile_case(args):
                       "launches": len(layers) * len(BATCHES)}))
 
 
+def prefill_int8(dev, gen, peaks):
+    """Secondary measurement: the int8 prefill GEMM (per-token int8 activations
+    x packed weights on the int8 tensor cores) at M = 4096 on the 7B-class
+    layer shapes.  Reports the GEMM alone (activations already quantised) and
+    with the activation quantiser, each from CUDA graphs of 10 launches."""
+    import torch
+    import penta_kernel as pk
+    rows = []
+    tot_ops = tot_gemm = tot_e2e = 0.0
+    for (K, N) in PREFILL_SHAPES:
+        w = torch.randn(N, K, device=dev, generator=gen) * 0.02
+        packed, _, s = pk.quantize_and_pack(w)
+        del w
+        x = torch.randn(PREFILL_M, K, device=dev, generator=gen).to(torch.bfloat16)
+        xq, s_x, rowsum = pk.quantize_activations_i8(x)
+        y = pk.penta_linear_i8_prequant(xq, s_x, rowsum, K, packed, s)
+        torch.cuda.synchronize()
+        times = []
+        for fn in (lambda: pk.penta_linear_i8_prequant(xq, s_x, rowsum, K, packed, s),
+                   lambda: pk.penta_linear_i8(x, packed, s, K)):
+            for _ in range(2):
+                fn()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(10):
+                    fn()
+            g.replay()
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1) / 10 * 1e-3)
+            del g
+        ops = 2.0 * PREFILL_M * N * K
+        tot_ops += ops
+        tot_gemm += times[0]
+        tot_e2e += times[1]
+        rows.append({"M": PREFILL_M, "K": K, "N": N, "gemm_us": round(times[0] * 1e6, 1),
+                     "tops": round(ops / times[0] / 1e12, 1), "with_quant_us": round(times[1] * 1e6, 1)})
+        del packed, x, xq, y
+    peak = 2.0 * peaks["bf16_tflops"]
+    return {"workload": f"int8 prefill GEMM, M={PREFILL_M}, K->N 4096->4096, 4096->11008, 11008->4096",
+            "value": round(tot_ops / tot_gemm / 1e12, 1), "unit": "TOPS",
+            "with_activation_quant": round(tot_ops / tot_e2e / 1e12, 1),
+            "roofline": {"bound": "tensor", "achieved": round(tot_ops / tot_gemm / 1e12, 1), "peak": round(peak, 1),
+                         "unit": "TOP/s", "frac": round(tot_ops / tot_gemm / 1e12 / peak, 4),
+                         "peak_source": "2 x measured dense bf16 (MEASURED_PEAKS.json); B200's dense int8 rate "
+                                        "is twice its bf16 rate", "kernel": "pn::dqmm_kernel<I8, 256>"},
+            "per_shape": rows}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -412,6 +471,10 @@ def run_ours(args):
     h2d = sum(2 * M * K for (M, K, N) in seq)
     d2h = sum(2 * M * N for (M, K, N) in seq)
 
+    prefill = None
+    if world == 1 and not args.no_prefill:
+        prefill = prefill_int8(dev, gen, peaks)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         rate, dt, kind, cores, desc = cpu_reference_rate(int(os.environ.get("PN_REF_ROWS", "2048")), 2, 1)
@@ -437,7 +500,9 @@ def run_ours(args):
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                     "path": "penta_kernel.penta_linear with pinned host x/y copies per call, eager"},
             "cpu_baseline": cpu,
-            "gpu_launches": len(seq) * args.steps,
+            # per product: the activation re-layout kernel and the dqmm kernel
+            "gpu_launches": 2 * len(seq) * args.steps,
+            "secondary": {"prefill_int8": prefill},
             "clocks": sampler.summary() if sampler else None,
         }
         print(json.dumps(line), flush=True)
@@ -455,6 +520,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the int8 prefill secondary measurement")
     ap.add_argument("--profile", action="store_true", help="small fixed case for ncu captures")
     args = ap.parse_args()
     if args.warmup < 3:
