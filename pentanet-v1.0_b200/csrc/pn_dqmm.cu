@@ -97,6 +97,9 @@ struct Cfg {
     static constexpr int kAParties = kUnpackGroups * T::kAPerKB;  // stage uses per round of groups
     static constexpr int kSAfit = (kTmemCols - kA0) / kAStageCols;
     static constexpr int kSA = (kSAfit >= 8 ? 8 : kSAfit) / kAParties * kAParties;
+    // A k-block's operand stages are released together, by one commit after
+    // its last MMA: one "slot" = kAPerKB consecutive stages.
+    static constexpr int kSlots = kSA / T::kAPerKB;
     static constexpr int kBudget = 200 * 1024;
     static constexpr int kSW = kXStageBytes >= 40 * 1024 ? 4 : (kXStageBytes >= 20 * 1024 ? 6 : 8);
     static constexpr int kSXfit = (kBudget - kSW * kWStageBytes) / kXStageBytes;
@@ -427,9 +430,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 mma_i8_ts_warp(d_tmem, a_col + j * 8, bdesc, idesc, acc);
                         }
                         first = false;
-                        tc_commit_warp(&empty_a[sa]);
                     }
                     if (!ok) break;
+                    tc_commit_warp(&empty_a[ik % C::kSlots]);
                     tc_commit_warp(&empty_x[sx]);
                 }
                 it = it0 + nkb;
@@ -502,8 +505,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     const uint32_t ua = ik * T::kAPerKB + hh;  // operand stage use
                     const int sa = ua % C::kSA;
-                    if (!warp_wait(&empty_a[sa], ((ua / C::kSA) & 1) ^ 1, abort_flag)) { ok = false; break; }
-                    tc_fence_after();
+                    if (hh == 0) {
+                        // the k-block's slot is free once the MMAs of its previous use are done
+                        if (!warp_wait(&empty_a[ik % C::kSlots], ((ik / C::kSlots) & 1) ^ 1, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                    }
                     const uint32_t a_addr = tmem_base + lane_base + C::kA0 + sa * C::kAStageCols;
                     uint32_t cols[40];
                     if constexpr (KIND == Kind::F16) {
