@@ -350,6 +350,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == kXLoadWarp) {
         // -------------------------------------------- activation loader ----
+        // (decode tiles read the pre-pass's output: wait for that grid)
+        if (C::kPerm) asm volatile("griddepcontrol.wait;" ::: "memory");
         uint32_t it = 0;
         bool ok = true;
         const int64_t u_end = range_begin(p, blockIdx.x + 1);
@@ -553,6 +555,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
 
             // ------------------------------------------------- epilogue ----
+            // Split-tile counters are zeroed by the decode pre-pass: wait for that grid.
+            if (C::kPerm) asm volatile("griddepcontrol.wait;" ::: "memory");
             // Issuer (it_item + a) % kIssuers accumulated k-blocks of this segment
             // iff a < its k-block count (segments are at least 2 k-blocks long).
             if (!warp_wait(acc_full, n_local & 1, abort_flag)) { ok = false; break; }
@@ -685,7 +689,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 // written (their accumulator columns are never read back).
 template <int BT>
 __global__ void __launch_bounds__(256) permute_x_kernel(const __nv_bfloat16* __restrict__ x, int M, int64_t K,
-                                                        int n_kb, uint8_t* __restrict__ out) {
+                                                        int n_kb, uint8_t* __restrict__ out, int* __restrict__ counters,
+                                                        int n_counters) {
+    // The GEMM launched after this kernel (programmatic dependent launch) may
+    // start its prologue and weight streaming now; it waits for this grid's
+    // results before it reads them.
+    asm volatile("griddepcontrol.launch_dependents;");
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_counters; i += gridDim.x * blockDim.x) counters[i] = 0;
     const int64_t kpad = (int64_t)n_kb * kKB;
     const int64_t total = (int64_t)M * kpad;
     for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
@@ -911,11 +921,20 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     prm.x_mode = x_mode;
     prm.packed_bytes = a.N * a.KP * 4;
     prm.xperm = ws + L.xperm;
+    // split-tile counters start at zero (the decode pre-pass zeroes them, else a memset)
+    const int n_counters = L.unit == 1 ? kUnpackWarps * (int)prm.n_items : 0;
     if (C::kPerm) {
         const int64_t total = a.M * (int64_t)prm.n_kb * kKB;
         const int blocks = (int)((total + 255) / 256 < 1024 ? (total + 255) / 256 : 1024);
         permute_x_kernel<BT><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(a.x), (int)a.M, a.K, prm.n_kb,
-                                                    ws + L.xperm);
+                                                    ws + L.xperm, prm.counters, n_counters);
+    } else if (n_counters > 0) {
+        cudaError_t e = cudaMemsetAsync(prm.counters, 0, sizeof(int) * (size_t)n_counters, s);
+        if (e != cudaSuccess) {
+            *err = e;
+            *why = "cudaMemsetAsync of the split-tile counters";
+            return PN_ERR_CUDA;
+        }
     }
     prm.scale = a.scale;
     prm.bias = static_cast<const __nv_bfloat16*>(a.bias);
@@ -939,16 +958,26 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
         if (dev >= 0 && dev < 64) attr_done[dev] = true;
     }
     const int grid = L.grid;
-    if (L.unit == 1) {
-        cudaError_t e = cudaMemsetAsync(prm.counters, 0, sizeof(int) * kUnpackWarps * (size_t)prm.n_items, s);
-        if (e != cudaSuccess) {
-            *err = e;
-            *why = "cudaMemsetAsync of the split-tile counters";
-            return PN_ERR_CUDA;
-        }
+    cudaError_t e;
+    if (C::kPerm) {
+        // Programmatic dependent launch: the GEMM's prologue, TMEM allocation
+        // and weight streaming overlap the activation pre-pass; the threads
+        // that read its results wait for it (griddepcontrol.wait).
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = C::kSmem;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, kern, xmap, wmap, prm);
+    } else {
+        kern<<<grid, kThreads, C::kSmem, s>>>(xmap, wmap, prm);
+        e = cudaGetLastError();
     }
-    kern<<<grid, kThreads, C::kSmem, s>>>(xmap, wmap, prm);
-    cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *err = e;
         *why = "kernel launch";
