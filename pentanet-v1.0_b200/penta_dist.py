@@ -48,11 +48,12 @@ def gather_columns(y_local: torch.Tensor, N: int, world: int, group=None,
     Requires N divisible by the world size (all 7B/70B shapes at P <= 8)."""
     M, n_loc = y_local.shape
     assert n_loc * world == N, "gather_columns needs equal shards"
-    buf = torch.empty(world, M, n_loc, dtype=y_local.dtype, device=y_local.device)
+    # rank-major concatenation along dim 0 (the layout every backend accepts)
+    buf = torch.empty(world * M, n_loc, dtype=y_local.dtype, device=y_local.device)
     dist.all_gather_into_tensor(buf, y_local.contiguous(), group=group)
     if out is None:
         out = torch.empty(M, N, dtype=y_local.dtype, device=y_local.device)
-    out.view(M, world, n_loc).copy_(buf.permute(1, 0, 2))
+    out.view(M, world, n_loc).copy_(buf.view(world, M, n_loc).permute(1, 0, 2))
     return out
 
 
