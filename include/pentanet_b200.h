@@ -141,6 +141,32 @@ int pn_linear_i8(const int8_t *xq, int64_t xq_pitch, const float *s_x, const int
 /* Number of SMs of the current device (used to size launches and shards). */
 int pn_device_sm_count(int *count_out);
 
+/* ---- output-sharded layers over the GPUs of one node (the reference has no
+ *      multi-GPU path; replaces "GEMV + NCCL all-gather") ------------------- */
+
+/* CUDA IPC: 64-byte handle of the allocation holding ptr (any cudaMalloc
+ * memory, e.g. a PyTorch tensor) and ptr's offset in it; map / unmap a peer's
+ * allocation (add the offset to the mapped base). */
+int pn_ipc_handle(const void *ptr, void *handle_out, size_t *offset_out);
+int pn_ipc_open(const void *handle, void **ptr_out);
+int pn_ipc_close(void *ptr);
+
+/* pn_linear_bf16 on this GPU's output rows [y_col0, y_col0 + N) of a layer,
+ * storing every output into each of the n_peers (<= 8) full-output buffers
+ * y_peers[r] (row stride ld_y elements; this GPU's and its peers'), so that
+ * after pn_peer_barrier every GPU holds the whole output.  M > 64 requires
+ * K % 8 == 0 and 16-byte aligned x. */
+int pn_linear_bf16_peers(const void *x, int64_t M, int64_t K, const int32_t *packed, int64_t N,
+                         int64_t K_packs, float scale, const void *bias, void *const *y_peers, int n_peers,
+                         int64_t ld_y, int64_t y_col0, int y_dtype, void *workspace, size_t workspace_bytes,
+                         void *stream);
+
+/* Cross-GPU barrier on `stream`: flags[r] is rank r's array of `world` ints
+ * (peer-mapped), gen this GPU's generation counter (device int, zero at
+ * start).  Returns once every rank has reached the same barrier; waits are
+ * bounded (PN_ERR_TIMEOUT in the device status word). */
+int pn_peer_barrier(int *const *flags, int world, int rank, int *gen, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

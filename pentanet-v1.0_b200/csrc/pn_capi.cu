@@ -149,22 +149,27 @@ size_t pn_linear_workspace_min_size(int kind, int64_t M, int64_t N, int64_t K) {
     return pn::linear_workspace_min_bytes(kind, M, N, K);
 }
 
-int pn_linear_bf16(const void* x, int64_t M, int64_t K, const int32_t* packed, int64_t N, int64_t K_packs,
-                   float scale, const void* bias, void* y, int y_dtype, void* workspace, size_t workspace_bytes,
-                   void* stream) {
-    if ((!x && M > 0) || (!packed && N > 0) || (!y && M > 0 && N > 0))
-        return fail(PN_ERR_ARG, "pn_linear_bf16: null pointer");
-    if (y_dtype != PN_BF16 && y_dtype != PN_F32) return fail(PN_ERR_DTYPE, "pn_linear_bf16: y_dtype %d", y_dtype);
+}  // extern "C"
+
+namespace {
+// pn_linear_bf16 and its output-sharded form share validation and launch.
+int linear_bf16_impl(const void* x, int64_t M, int64_t K, const int32_t* packed, int64_t N, int64_t K_packs,
+                     float scale, const void* bias, void* y, int y_dtype, void* workspace, size_t workspace_bytes,
+                     void* stream, void* const* y_peers, int n_peers, int64_t ld_y, int64_t y_col0,
+                     const char* name) {
+    if ((!x && M > 0) || (!packed && N > 0) || (!y && n_peers == 0 && M > 0 && N > 0))
+        return fail(PN_ERR_ARG, "%s: null pointer", name);
+    if (y_dtype != PN_BF16 && y_dtype != PN_F32) return fail(PN_ERR_DTYPE, "%s: y_dtype %d", name, y_dtype);
     if (M < 0 || N < 0 || K < 1 || M > 0x7fffffff || N > 0x7fffffff)
-        return fail(PN_ERR_SHAPE, "pn_linear_bf16: M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+        return fail(PN_ERR_SHAPE, "%s: M=%lld N=%lld K=%lld", name, (long long)M, (long long)N, (long long)K);
     if (K_packs != k_packs(K))
-        return fail(PN_ERR_SHAPE, "pn_linear_bf16: activation K=%lld needs K_packs=%lld, got %lld", (long long)K,
+        return fail(PN_ERR_SHAPE, "%s: activation K=%lld needs K_packs=%lld, got %lld", name, (long long)K,
                     (long long)k_packs(K), (long long)K_packs);
     if (!aligned(x, 2) || !aligned(packed, 16) || !aligned(y, y_dtype == PN_F32 ? 4 : 2) || !aligned(bias, 2))
-        return fail(PN_ERR_ALIGN, "pn_linear_bf16: misaligned pointer (packed weights need 16-byte alignment)");
+        return fail(PN_ERR_ALIGN, "%s: misaligned pointer (packed weights need 16-byte alignment)", name);
     const size_t need = pn::linear_workspace_min_bytes(PN_BF16, M, N, K);
     if (need > 0 && (!workspace || workspace_bytes < need))
-        return fail(PN_ERR_WORKSPACE, "pn_linear_bf16: workspace needs at least %zu bytes (%zu recommended)", need,
+        return fail(PN_ERR_WORKSPACE, "%s: workspace needs at least %zu bytes (%zu recommended)", name, need,
                     pn::linear_workspace_bytes(PN_BF16, M, N, K));
     if (int st = check_device()) return st;
     if (M == 0 || N == 0) return ok();
@@ -183,6 +188,10 @@ int pn_linear_bf16(const void* x, int64_t M, int64_t K, const int32_t* packed, i
     a.y_dtype = y_dtype;
     a.workspace = workspace;
     a.workspace_bytes = workspace_bytes;
+    a.n_peers = n_peers;
+    for (int r = 0; r < n_peers && r < 8; ++r) a.y_peers[r] = y_peers[r];
+    a.ld_y = ld_y;
+    a.y_col0 = y_col0;
     // Decode-sized M reads x with plain loads (any K); larger M loads it by TMA,
     // which needs 16-byte rows.
     if (M > 64 && (K % 8 != 0 || !aligned(x, 16))) {
@@ -193,8 +202,18 @@ int pn_linear_bf16(const void* x, int64_t M, int64_t K, const int32_t* packed, i
     const char* why;
     const int st = pn::launch_linear(a, (cudaStream_t)stream, &ce, &why);
     if (st == PN_ERR_CUDA) return cuda_fail(ce, why);
-    if (st != PN_OK) return fail(st, "pn_linear_bf16: %s", why);
+    if (st != PN_OK) return fail(st, "%s: %s", name, why);
     return ok();
+}
+}  // namespace
+
+extern "C" {
+
+int pn_linear_bf16(const void* x, int64_t M, int64_t K, const int32_t* packed, int64_t N, int64_t K_packs,
+                   float scale, const void* bias, void* y, int y_dtype, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+    return linear_bf16_impl(x, M, K, packed, N, K_packs, scale, bias, y, y_dtype, workspace, workspace_bytes, stream,
+                            nullptr, 0, 0, 0, "pn_linear_bf16");
 }
 
 int64_t pn_act_i8_pitch(int64_t K) { return pn::act_i8_pitch(K); }

@@ -130,7 +130,9 @@ struct DqmmParams {
     int64_t packed_bytes;
     float scale;
     const __nv_bfloat16* bias;
-    void* y;
+    void* y_out[8];        // output buffers (one, or one per GPU of an output-sharded layer)
+    int n_out;
+    int64_t ld_y, y_col0;  // row stride of the outputs and this shard's first column
     int y_f32;
     int32_t* acc_out;
     const float* s_x;
@@ -580,14 +582,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const float f = __fmul_rn(p.scale, __ldg(p.s_x + m));
                         yv = __fmul_rn((float)acc_i, f);
                     }
-                    if (p.y != nullptr) {
+                    if (p.n_out > 0) {
+                        const int64_t off = (int64_t)m * p.ld_y + p.y_col0 + n;
                         if (p.y_f32) {
                             if (p.bias) yv = __fadd_rn(yv, bias_f);
-                            static_cast<float*>(p.y)[(int64_t)m * p.N + n] = yv;
+                            for (int r = 0; r < p.n_out; ++r) static_cast<float*>(p.y_out[r])[off] = yv;
                         } else {
                             __nv_bfloat16 t = __float2bfloat16_rn(yv);
                             if (p.bias) t = __float2bfloat16_rn(__fadd_rn(__bfloat162float(t), bias_f));
-                            static_cast<__nv_bfloat16*>(p.y)[(int64_t)m * p.N + n] = t;
+                            for (int r = 0; r < p.n_out; ++r) static_cast<__nv_bfloat16*>(p.y_out[r])[off] = t;
                         }
                     }
                 }
@@ -676,6 +679,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
+    // Outputs written into other GPUs' memory are ordered before this grid's
+    // completion, which the cross-GPU barrier after the product relies on.
+    if (p.n_out > 1 && warp < kUnpackWarps) __threadfence_system();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -938,7 +944,17 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     }
     prm.scale = a.scale;
     prm.bias = static_cast<const __nv_bfloat16*>(a.bias);
-    prm.y = a.y;
+    if (a.n_peers > 0) {
+        prm.n_out = a.n_peers;
+        for (int r = 0; r < 8; ++r) prm.y_out[r] = r < a.n_peers ? a.y_peers[r] : nullptr;
+        prm.ld_y = a.ld_y;
+        prm.y_col0 = a.y_col0;
+    } else {
+        prm.n_out = a.y != nullptr ? 1 : 0;
+        for (int r = 0; r < 8; ++r) prm.y_out[r] = r == 0 ? a.y : nullptr;
+        prm.ld_y = a.N;
+        prm.y_col0 = 0;
+    }
     prm.y_f32 = a.y_dtype == PN_F32;
     prm.acc_out = a.acc_out;
     prm.s_x = a.s_x;

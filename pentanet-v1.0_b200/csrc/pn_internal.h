@@ -27,6 +27,12 @@ struct LinearArgs {
     const void* bias;         // bf16 (N) or null
     void* y;                  // (M, N) or null (int8 path only)
     int y_dtype;              // PN_BF16 / PN_F32
+    // Output-sharded layers: when n_peers > 0 the outputs go to every buffer
+    // in y_peers (this GPU's and its peers', row stride ld_y elements, this
+    // shard's columns starting at y_col0) instead of y.
+    void* y_peers[8];
+    int n_peers;
+    int64_t ld_y, y_col0;
     int32_t* acc_out;         // int8 path: (M, N) int32 or null
     const float* s_x;         // int8 path
     const int32_t* rowsum;    // int8 path

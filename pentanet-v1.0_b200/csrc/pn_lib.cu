@@ -11,3 +11,4 @@
 #include "pn_simt.cu"
 #include "pn_capi.cu"
 #include "pn_static_ws.cu"
+#include "pn_peer.cu"
