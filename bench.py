@@ -338,13 +338,25 @@ def run_ours(args):
     xs = {(M, K): torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16) for (M, K, _) in launches_per_step()}
 
     seq = launches_per_step()
+    # N > 1: each product's GEMM stores its output columns into every GPU's
+    # full-output buffer (peer memory), then a cross-GPU barrier kernel.
+    peers = pd.PeerGroup() if world > 1 else None
+    outs_peer = [peers.buffer((M, N), torch.bfloat16) for (M, K, N) in seq] if peers else None
+    col0 = {(K, N): pd.shard_range(N, rank, world)[0] for (K, N) in SHAPES}
+
+    def product(l: int, c: int, barrier: bool = True):
+        M, K, N = seq[l]
+        if peers is None:
+            return pk.penta_linear(xs[(M, K)], packed[(K, N)][c], scales[(K, N)], K)
+        pd.linear_peers(xs[(M, K)], packed[(K, N)][c], scales[(K, N)], K, col0[(K, N)], outs_peer[l][1], N)
+        if barrier:
+            peers.barrier()
+        return outs_peer[l][0]
 
     def run_step(i: int, outs=None):
         for l, (M, K, N) in enumerate(seq):
             c = ((6 * i + l) // 2) % COPIES
-            y = pk.penta_linear(xs[(M, K)], packed[(K, N)][c], scales[(K, N)], K)
-            if world > 1:
-                y = pd.gather_columns(y, N, world)
+            y = product(l, c)
             if outs is not None:
                 outs.append(y)
 
@@ -352,9 +364,10 @@ def run_ours(args):
         run_step(i)
     torch.cuda.synchronize()
 
-    # Graph capture (N = 1): one graph per step phase removes host launch cost.
+    # One CUDA graph per step phase removes host launch cost (at N > 1 the
+    # graphs hold the GEMMs and the cross-GPU barrier kernels, no NCCL calls).
     graphs = []
-    if world == 1:
+    if True:
         for ph in range(4):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
@@ -399,33 +412,26 @@ def run_ours(args):
 
     # ---- per-launch kernel durations (roofline): each (shape, M) alone, 20 launches, rotating copies
     per = []
-    for (M, K, N) in seq:
+    for l, (M, K, N) in enumerate(seq):
         n_loc = packed[(K, N)][0].shape[0]
         reps = 20
-        if world == 1:
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                for r in range(reps):
-                    pk.penta_linear(xs[(M, K)], packed[(K, N)][r % COPIES], scales[(K, N)], K)
-            g.replay()
-            torch.cuda.synchronize()
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            g.replay()
-            e1.record(stream)
-            torch.cuda.synchronize()
-            dur = e0.elapsed_time(e1) / reps
-            del g
-        else:
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
+        # the local GEMM alone (its peer stores included, no barrier)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
             for r in range(reps):
-                pk.penta_linear(xs[(M, K)], packed[(K, N)][r % COPIES], scales[(K, N)], K)
-            e1.record(stream)
-            torch.cuda.synchronize()
-            dur = e0.elapsed_time(e1) / reps
+                product(l, r % COPIES, barrier=False)
+        g.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        dur = e0.elapsed_time(e1) / reps
+        del g
         b = alg_bytes(M, K, n_loc)
         per.append({"M": M, "K": K, "N": N, "rows_local": n_loc, "us": round(dur * 1e3, 2),
                     "gbs": round(b / (dur * 1e-3) / 1e9, 1)})
@@ -444,9 +450,12 @@ def run_ours(args):
         for l, (M, K, N) in enumerate(seq):
             c = ((6 * i + l) // 2) % COPIES
             xd[(M, K)].copy_(xh[(M, K)], non_blocking=True)
-            y = pk.penta_linear(xd[(M, K)], packed[(K, N)][c], scales[(K, N)], K)
-            if world > 1:
-                y = pd.gather_columns(y, N, world)
+            if peers is None:
+                y = pk.penta_linear(xd[(M, K)], packed[(K, N)][c], scales[(K, N)], K)
+            else:
+                pd.linear_peers(xd[(M, K)], packed[(K, N)][c], scales[(K, N)], K, col0[(K, N)], outs_peer[l][1], N)
+                peers.barrier()
+                y = outs_peer[l][0]
             yh[(M, K, N)].copy_(y, non_blocking=True)
 
     e2e_steps = max(1, min(args.steps, 200))
@@ -490,18 +499,22 @@ def run_ours(args):
                        "activations": "bf16 N(0,1)",
                        "l2": f"inputs larger than L2: {COPIES} weight copies per shape rotated "
                              f"({COPIES * 2 * 94} MB); a buffer is reused after >= 7 other 94 MB launches",
-                       "parallelism": "single GPU" if world == 1 else f"output rows sharded x{world} + NCCL all-gather",
-                       "timing": "CUDA graphs of one step" if world == 1 else "eager launches"},
+                       "parallelism": "single GPU" if world == 1 else
+                       f"output rows sharded x{world}; outputs stored into every GPU's buffer by the GEMM "
+                       f"(NVLink peer stores) + cross-GPU barrier kernel",
+                       "timing": "CUDA graphs of one step"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
                          "peak_source": peaks["source"], "kernel": "pn::dqmm_kernel<F16, BT>",
                          "per_launch": per},
             "e2e": {"value": round(e2e_val, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                    "path": "penta_kernel.penta_linear with pinned host x/y copies per call, eager"},
+                    "path": ("penta_kernel.penta_linear" if world == 1 else "penta_dist.linear_peers + barrier")
+                            + " with pinned host x/y copies per call, eager"},
             "cpu_baseline": cpu,
             # per product: the activation re-layout kernel and the dqmm kernel
-            "gpu_launches": 2 * len(seq) * args.steps,
+            # (+ the cross-GPU barrier kernel when sharded)
+            "gpu_launches": (2 if world == 1 else 3) * len(seq) * args.steps,
             "secondary": {"prefill_int8": prefill},
             "clocks": sampler.summary() if sampler else None,
         }
@@ -509,7 +522,9 @@ def run_ours(args):
 
     graphs.clear()
     if world > 1:
+        torch.cuda.synchronize()
         dist.barrier()
+        peers.close()
         dist.destroy_process_group()
 
 

@@ -122,7 +122,12 @@ struct DqmmParams {
     int n_row_tiles, n_items, n_kb;
     int64_t total_pairs;   // n_items * (n_kb / 2): the flattened (tile, k-block pair) work
     int unit;              // pairs per indivisible unit: 1 (tiles may split) or n_kb / 2 (whole tiles)
-    uint32_t* partials;    // [gridDim.x][2][128][BT] fp32 / int32 partial accumulators
+    // Split tiles.  16-token tiles: one sum buffer per split tile,
+    // [gridDim.x][128][acc_cols] int64 fixed point (bf16 path) / int32,
+    // added with atomics.  Larger tiles: per-CTA partials
+    // [gridDim.x][2][128][BT], summed by the last contributor.
+    void* accbuf;
+    int acc_cols;          // columns of a 16-token tile's sum buffer: min(16, M)
     int* counters;         // [n_items][16 unpack warps] arrival counters of split tiles (zeroed by the host)
     int w_pad;      // weights read from a 16-byte-pitch copy in the workspace (unused by the kernel)
     int x_mode;     // activation staging: 0 one 3D TMA box per k-block, 1 one 2D box per MMA K-step
@@ -263,6 +268,19 @@ __device__ __forceinline__ Seg segment_at(const DqmmParams& p, int64_t u, int64_
     g.kb1 = 2 * pe;
     g.whole = pb == 0 && pe == P;
     return g;
+}
+
+// Split 16-token tiles are summed with integer atomics, so the result does not
+// depend on the order in which contributors arrive: int32 accumulators add exactly,
+// and fp32 partials are added as 64-bit fixed point with 2^-24 resolution
+// (exact for every partial of magnitude >= 2^-1, error <= 2^-25 otherwise;
+// range +-2^39).  The sum is converted back with one rounding to fp32.
+constexpr float kFixScale = 16777216.0f;  // 2^24
+__device__ __forceinline__ void red_add(long long* p, long long v) {
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void red_add(int* p, int v) {
+    asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 template <Kind KIND, int BT>
@@ -601,9 +619,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 else
                     d = (uint32_t)((int)d + (int)v);
             };
-            // Split tiles publish partials to slot 0 (the CTA's first tile) or 1.
+            // Split tiles: 16-token tiles add into the sum buffer of the tile's
+            // first contributor (each CTA is the first contributor of at most
+            // one split tile); larger tiles publish partials to this CTA's
+            // slot 0 (its first tile) or 1.
+            constexpr bool kRedSum = BT <= 16;
+            const int Pp = p.n_kb / 2;
+            const int c_first = g.whole ? 0 : owner_of(p, (int64_t)g.tile * Pp);
+            const size_t acc_base = ((size_t)c_first * kRows + row) * p.acc_cols;
             const int slot = g.tile == my_first_tile ? 0 : 1;
-            uint32_t* part = p.partials + ((size_t)(blockIdx.x * 2 + slot) * kRows + row) * BT;
+            uint32_t* part = static_cast<uint32_t*>(p.accbuf) + ((size_t)(blockIdx.x * 2 + slot) * kRows + row) * BT;
             // This thread's accumulator columns: chunks c0 = 16*half + 64*i.
 #pragma unroll 1
             for (int c0 = 16 * half; c0 < BT; c0 += 16 * kUnpackGroups) {
@@ -619,6 +644,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (g.whole) {
                     finish(c0, acc);
+                } else if constexpr (kRedSum) {
+                    // (griddepcontrol.wait above: the decode pre-pass zeroed the sums)
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        if (m0 + c0 + j >= p.M) break;
+                        if constexpr (KIND == Kind::F16)
+                            red_add(static_cast<long long*>(p.accbuf) + acc_base + c0 + j,
+                                    __float2ll_rn(__uint_as_float(acc[j]) * kFixScale));
+                        else
+                            red_add(static_cast<int*>(p.accbuf) + acc_base + c0 + j, (int)acc[j]);
+                    }
                 } else {
 #pragma unroll
                     for (int j = 0; j < 16; j += 4)
@@ -633,11 +669,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!g.whole) {
                 // Each warp owns a fixed slice of the tile (its 32 rows x its
                 // column chunks) in every contributing CTA, so arrivals are
-                // counted per (tile, warp): the last warp to publish its slice
-                // sums that slice over all contributors, in CTA order.
-                const int P = p.n_kb / 2;
-                const int c_first = owner_of(p, (int64_t)g.tile * P);
-                const int c_last = owner_of(p, (int64_t)g.tile * P + P - 1);
+                // counted per (tile, warp): the last warp to add (or publish)
+                // its slice turns that slice of the sum into outputs.
+                const int c_last = owner_of(p, (int64_t)g.tile * Pp + Pp - 1);
                 __threadfence();
                 __syncwarp();
                 int last = 0;
@@ -653,22 +687,41 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int c0 = 16 * half; c0 < BT; c0 += 16 * kUnpackGroups) {
                         if (m0 + c0 >= p.M) break;
                         uint32_t acc[16];
-                        for (int c = c_first; c <= c_last; ++c) {
-                            const int slot_c = g.tile == (int)(range_begin(p, c) / P) ? 0 : 1;
-                            const uint32_t* pc = p.partials + ((size_t)(c * 2 + slot_c) * kRows + row) * BT + c0;
+                        if constexpr (kRedSum) {
 #pragma unroll
-                            for (int j = 0; j < 16; j += 4) {
-                                const uint4 q4 = __ldcg(reinterpret_cast<const uint4*>(pc + j));
-                                if (c == c_first) {
-                                    acc[j] = q4.x;
-                                    acc[j + 1] = q4.y;
-                                    acc[j + 2] = q4.z;
-                                    acc[j + 3] = q4.w;
-                                } else {
-                                    add_into(acc[j], q4.x);
-                                    add_into(acc[j + 1], q4.y);
-                                    add_into(acc[j + 2], q4.z);
-                                    add_into(acc[j + 3], q4.w);
+                            for (int j = 0; j < 16; ++j) {
+                                acc[j] = 0;
+                                if (m0 + c0 + j < p.M) {
+                                    if constexpr (KIND == Kind::F16) {
+                                        const long long v =
+                                            __ldcg(static_cast<const long long*>(p.accbuf) + acc_base + c0 + j);
+                                        acc[j] = __float_as_uint(__ll2float_rn(v) * (1.0f / kFixScale));
+                                    } else {
+                                        acc[j] = (uint32_t)__ldcg(static_cast<const int*>(p.accbuf) + acc_base + c0 + j);
+                                    }
+                                }
+                            }
+                        } else {
+                            // CTA c's partials sit in its slot 0 when the tile is its
+                            // first one, else in slot 1; summed in CTA order.
+                            for (int c = c_first; c <= c_last; ++c) {
+                                const int slot_c = g.tile == (int)(range_begin(p, c) / Pp) ? 0 : 1;
+                                const uint32_t* pc = static_cast<const uint32_t*>(p.accbuf) +
+                                                     ((size_t)(c * 2 + slot_c) * kRows + row) * BT + c0;
+#pragma unroll
+                                for (int j = 0; j < 16; j += 4) {
+                                    const uint4 q4 = __ldcg(reinterpret_cast<const uint4*>(pc + j));
+                                    if (c == c_first) {
+                                        acc[j] = q4.x;
+                                        acc[j + 1] = q4.y;
+                                        acc[j + 2] = q4.z;
+                                        acc[j + 3] = q4.w;
+                                    } else {
+                                        add_into(acc[j], q4.x);
+                                        add_into(acc[j + 1], q4.y);
+                                        add_into(acc[j + 2], q4.z);
+                                        add_into(acc[j + 3], q4.w);
+                                    }
                                 }
                             }
                         }
@@ -695,13 +748,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 // written (their accumulator columns are never read back).
 template <int BT>
 __global__ void __launch_bounds__(256) permute_x_kernel(const __nv_bfloat16* __restrict__ x, int M, int64_t K,
-                                                        int n_kb, uint8_t* __restrict__ out, int* __restrict__ counters,
-                                                        int n_counters) {
+                                                        int n_kb, uint8_t* __restrict__ out, uint4* __restrict__ zero,
+                                                        int64_t n_zero16) {
     // The GEMM launched after this kernel (programmatic dependent launch) may
     // start its prologue and weight streaming now; it waits for this grid's
     // results before it reads them.
     asm volatile("griddepcontrol.launch_dependents;");
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_counters; i += gridDim.x * blockDim.x) counters[i] = 0;
+    // the GEMM's split-tile counters and sums start at zero
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_zero16; i += (int64_t)gridDim.x * blockDim.x)
+        zero[i] = make_uint4(0, 0, 0, 0);
     const int64_t kpad = (int64_t)n_kb * kKB;
     const int64_t total = (int64_t)M * kpad;
     for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
@@ -774,14 +829,16 @@ static int token_tile(int kind, int64_t M) {
 // Workspace sections, each 256-byte aligned:
 //   [decode activation slabs (bf16, M <= 64)]
 //   [weights re-pitched to 16-byte rows (K_packs % 4 != 0)]
-//   [split-tile partials: grid x 2 x 128 x BT x 4 bytes]
 //   [split-tile arrival counters: one int per tile and unpack warp]
+//   [split-tile sums (16-token tiles): grid x 128 x min(16, M), int64 (bf16) /
+//    int32 (int8) -- zeroed with the counters in one pass -- or partials
+//    (larger tiles): grid x 2 x 128 x BT x 4 bytes]
 // Tiles split across CTAs only while there are few of them per SM; with many
 // tiles whole-tile ranges already balance to within one tile.
 struct WsLayout {
-    size_t xperm, wpitch, partials, counters, total;
+    size_t xperm, wpitch, counters, accbuf, zero_bytes, total;
     int64_t n_items, total_pairs;
-    int grid, bt, n_kb, unit;
+    int grid, bt, n_kb, unit, acc_cols;
 };
 static WsLayout ws_layout(int kind, int64_t M, int64_t N, int64_t K, bool allow_split) {
     WsLayout w{};
@@ -801,12 +858,20 @@ static WsLayout ws_layout(int kind, int64_t M, int64_t N, int64_t K, bool allow_
     if (kind == PN_BF16 && M >= 1 && M <= 64) off += round256((size_t)w.n_kb * w.bt * 32 * 10);
     w.wpitch = off;
     if (KP % 4 != 0) off += round256((size_t)N * w_pitch(KP) * 4);
-    w.partials = off;
+    w.acc_cols = (int)(M < 16 ? M : 16);
     w.counters = off;
+    w.accbuf = off;
+    w.zero_bytes = 0;
     if (split) {
-        off += round256((size_t)w.grid * 2 * kRows * w.bt * 4);
-        w.counters = off;
         off += round256((size_t)w.n_items * kUnpackWarps * 4);
+        w.accbuf = off;
+        if (w.bt <= 16) {
+            off += round256((size_t)w.grid * kRows * w.acc_cols * (kind == PN_BF16 ? 8 : 4));
+            w.zero_bytes = off - w.counters;  // counters and sums
+        } else {
+            w.zero_bytes = off - w.counters;  // counters only
+            off += round256((size_t)w.grid * 2 * kRows * w.bt * 4);
+        }
     }
     w.total = off;
     return w;
@@ -920,7 +985,8 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     prm.n_items = prm.n_row_tiles * n_tok_tiles;
     prm.total_pairs = L.total_pairs;
     prm.unit = L.unit;
-    prm.partials = reinterpret_cast<uint32_t*>(ws + L.partials);
+    prm.accbuf = ws + L.accbuf;
+    prm.acc_cols = L.acc_cols;
     prm.counters = reinterpret_cast<int*>(ws + L.counters);
     prm.n_kb = n_kblocks(a.KP);
     prm.w_pad = repitch;
@@ -928,14 +994,16 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     prm.packed_bytes = a.N * a.KP * 4;
     prm.xperm = ws + L.xperm;
     // split-tile counters start at zero (the decode pre-pass zeroes them, else a memset)
-    const int n_counters = L.unit == 1 ? kUnpackWarps * (int)prm.n_items : 0;
+    const int64_t n_zero16 = L.unit == 1 ? (int64_t)(L.zero_bytes / 16) : 0;
     if (C::kPerm) {
         const int64_t total = a.M * (int64_t)prm.n_kb * kKB;
-        const int blocks = (int)((total + 255) / 256 < 1024 ? (total + 255) / 256 : 1024);
+        int64_t want = (total + 255) / 256;
+        if (n_zero16 / 1024 > want) want = n_zero16 / 1024;  // ~4 zeroing stores per thread
+        const int blocks = (int)(want < 1024 ? (want > 0 ? want : 1) : 1024);
         permute_x_kernel<BT><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(a.x), (int)a.M, a.K, prm.n_kb,
-                                                    ws + L.xperm, prm.counters, n_counters);
-    } else if (n_counters > 0) {
-        cudaError_t e = cudaMemsetAsync(prm.counters, 0, sizeof(int) * (size_t)n_counters, s);
+                                                    ws + L.xperm, reinterpret_cast<uint4*>(ws + L.counters), n_zero16);
+    } else if (n_zero16 > 0) {
+        cudaError_t e = cudaMemsetAsync(ws + L.counters, 0, L.zero_bytes, s);
         if (e != cudaSuccess) {
             *err = e;
             *why = "cudaMemsetAsync of the split-tile counters";
