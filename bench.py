@@ -305,6 +305,37 @@ def prefill_int8(dev, gen, peaks):
             "per_shape": rows}
 
 
+def pentagpt_forward(dev):
+    """Secondary measurement: PentaGPT-124M forward (prefill) tokens/s -- 12
+    layers, d 768, every projection packed, batch 32 x 1024 random token ids,
+    random weights from seed 42; last-position logits as the reference's
+    inference forward.  bf16 projections (the parity path) and the per-token
+    int8 projections."""
+    import torch
+    from pentagpt import PentaGPTFast
+    B, T = 32, 1024
+    idx = torch.randint(0, 50257, (B, T), generator=torch.Generator().manual_seed(42)).to(dev)
+    res = {"workload": "PentaGPT-124M forward, batch 32 x seq 1024, random init seed 42", "unit": "tokens/s"}
+    for name, aq in (("bf16", None), ("int8", "int8")):
+        model = PentaGPTFast.random(seed=42, device=dev, act_quant=aq)
+        model(idx)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        reps = 5
+        e0.record()
+        for _ in range(reps):
+            model(idx)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        res[name] = {"tokens_per_s": round(B * T / (ms * 1e-3)), "ms_per_forward": round(ms, 2)}
+        del model
+        torch.cuda.empty_cache()
+    res["value"] = res["bf16"]["tokens_per_s"]
+    return res
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -481,8 +512,10 @@ def run_ours(args):
     d2h = sum(2 * M * N for (M, K, N) in seq)
 
     prefill = None
+    gpt = None
     if world == 1 and not args.no_prefill:
         prefill = prefill_int8(dev, gen, peaks)
+        gpt = pentagpt_forward(dev)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -515,7 +548,7 @@ def run_ours(args):
             # per product: the activation re-layout kernel and the dqmm kernel
             # (+ the cross-GPU barrier kernel when sharded)
             "gpu_launches": (2 if world == 1 else 3) * len(seq) * args.steps,
-            "secondary": {"prefill_int8": prefill},
+            "secondary": {"prefill_int8": prefill, "pentagpt_124m_fwd": gpt},
             "clocks": sampler.summary() if sampler else None,
         }
         print(json.dumps(line), flush=True)
