@@ -28,6 +28,7 @@
 
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 namespace pn {
 
@@ -486,6 +487,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t u_begin = range_begin(p, blockIdx.x);
         const int64_t u_end = range_begin(p, blockIdx.x + 1);
         const int my_first_tile = (int)(u_begin / (p.n_kb / 2));
+        // single-output destination (n_out == 1: row stride N, first column 0)
+        float* const y0f = static_cast<float*>(p.y_out[0]);
+        __nv_bfloat16* const y0h = static_cast<__nv_bfloat16*>(p.y_out[0]);
         for (int64_t u = u_begin; u < u_end && ok; ++n_local) {
             const Seg g = segment_at(p, u, u_end);
             u += (g.kb1 - g.kb0) / 2;
@@ -585,7 +589,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             float bias_f = 0.0f;
             if (p.bias != nullptr && n < p.N) bias_f = __bfloat162float(p.bias[n]);
             // Final epilogue of 16 accumulator columns starting at c0.
-            auto finish = [&](int c0, const uint32_t (&acc)[16]) {
+            // MULTI: output-sharded layers store into every GPU's buffer; the
+            // common single-output case is compiled separately.
+            auto finish_t = [&](auto multi, int c0, const uint32_t (&acc)[16]) {
+                constexpr bool MULTI = decltype(multi)::value;
                 if (n >= p.N) return;
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
@@ -601,17 +608,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                         yv = __fmul_rn((float)acc_i, f);
                     }
                     if (p.n_out > 0) {
-                        const int64_t off = (int64_t)m * p.ld_y + p.y_col0 + n;
                         if (p.y_f32) {
                             if (p.bias) yv = __fadd_rn(yv, bias_f);
-                            for (int r = 0; r < p.n_out; ++r) static_cast<float*>(p.y_out[r])[off] = yv;
+                            if constexpr (MULTI) {
+                                const int64_t off = (int64_t)m * p.ld_y + p.y_col0 + n;
+                                for (int r = 0; r < p.n_out; ++r) static_cast<float*>(p.y_out[r])[off] = yv;
+                            } else {
+                                y0f[(int64_t)m * p.N + n] = yv;
+                            }
                         } else {
                             __nv_bfloat16 t = __float2bfloat16_rn(yv);
                             if (p.bias) t = __float2bfloat16_rn(__fadd_rn(__bfloat162float(t), bias_f));
-                            for (int r = 0; r < p.n_out; ++r) static_cast<__nv_bfloat16*>(p.y_out[r])[off] = t;
+                            if constexpr (MULTI) {
+                                const int64_t off = (int64_t)m * p.ld_y + p.y_col0 + n;
+                                for (int r = 0; r < p.n_out; ++r) static_cast<__nv_bfloat16*>(p.y_out[r])[off] = t;
+                            } else {
+                                y0h[(int64_t)m * p.N + n] = t;
+                            }
                         }
                     }
                 }
+            };
+            auto finish = [&](int c0, const uint32_t (&acc)[16]) {
+                if (p.n_out > 1)
+                    finish_t(std::true_type{}, c0, acc);
+                else
+                    finish_t(std::false_type{}, c0, acc);
             };
             auto add_into = [&](uint32_t& d, uint32_t v) {
                 if constexpr (KIND == Kind::F16)
