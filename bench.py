@@ -336,6 +336,26 @@ def pentagpt_forward(dev):
     return res
 
 
+def run_profile_prefill(args):
+    """Small case for ncu: the int8 prefill GEMM at M = 4096, K = N = 4096,
+    three warm-up launches and one measured launch (activations quantised
+    beforehand)."""
+    import torch
+    import penta_kernel as pk
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(1234)
+    K = N = M = 4096
+    w = torch.randn(N, K, device=dev, generator=gen) * 0.02
+    packed, _, s = pk.quantize_and_pack(w)
+    del w
+    x = torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16)
+    xq, s_x, rowsum = pk.quantize_activations_i8(x)
+    for _ in range(4):
+        pk.penta_linear_i8_prequant(xq, s_x, rowsum, K, packed, s)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": "int8 prefill 4096x4096x4096", "warmup_launches": 3, "launches": 1}))
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -570,9 +590,13 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-prefill", action="store_true", help="skip the int8 prefill secondary measurement")
     ap.add_argument("--profile", action="store_true", help="small fixed case for ncu captures")
+    ap.add_argument("--profile-prefill", action="store_true", help="int8 prefill case for ncu captures")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.profile_prefill:
+        run_profile_prefill(args)
+        return
     if args.profile:
         run_profile_case(args)
     elif args.impl == "reference":

@@ -629,8 +629,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             };
+            // Common case in one straight pass: one bf16 output, no bias, no
+            // accumulator copy, all 16 tokens of the chunk present.
+            auto finish_fast = [&](int c0, const uint32_t (&acc)[16]) {
+                if (n >= p.N) return;
+                __nv_bfloat16* yp = y0h + (int64_t)(m0 + c0) * p.N + n;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    float yv;
+                    if constexpr (KIND == Kind::F16) {
+                        yv = __fmul_rn(__uint_as_float(acc[j]), p.scale);
+                    } else {
+                        const int m = m0 + c0 + j;
+                        const int acc_i = (int)acc[j] - 2 * __ldg(p.rowsum + m);
+                        yv = __fmul_rn((float)acc_i, __fmul_rn(p.scale, __ldg(p.s_x + m)));
+                    }
+                    yp[(int64_t)j * p.N] = __float2bfloat16_rn(yv);
+                }
+            };
+            const bool fast_out = p.n_out == 1 && !p.y_f32 && p.bias == nullptr && p.acc_out == nullptr;
             auto finish = [&](int c0, const uint32_t (&acc)[16]) {
-                if (p.n_out > 1)
+                if (fast_out && m0 + c0 + 16 <= p.M)
+                    finish_fast(c0, acc);
+                else if (p.n_out > 1)
                     finish_t(std::true_type{}, c0, acc);
                 else
                     finish_t(std::false_type{}, c0, acc);
