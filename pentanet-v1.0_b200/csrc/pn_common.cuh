@@ -295,6 +295,30 @@ __device__ __forceinline__ uint64_t smem_desc_sw32(const void* slab) {
     return d;
 }
 
+// The same for K-major operands in 128- and 64-byte swizzled boxes (8-row
+// groups of 128- or 64-byte rows, box base aligned to the 8-row group).  An
+// MMA K-step inside a swizzled row starts at the row's start plus its byte
+// offset; the swizzle is applied to the computed addresses, so the offset
+// is simply added to the start address.
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void* start) {
+    const uint64_t addr = smem_u32(start);
+    uint64_t d = (addr >> 4) & 0x3FFFull;
+    d |= 1ull << 16;
+    d |= (1024ull >> 4) << 32;  // stride byte offset: 8 rows x 128 B
+    d |= 1ull << 46;
+    d |= 2ull << 61;            // layout: SWIZZLE_128B
+    return d;
+}
+__device__ __forceinline__ uint64_t smem_desc_sw64(const void* start) {
+    const uint64_t addr = smem_u32(start);
+    uint64_t d = (addr >> 4) & 0x3FFFull;
+    d |= 1ull << 16;
+    d |= (512ull >> 4) << 32;   // stride byte offset: 8 rows x 64 B
+    d |= 1ull << 46;
+    d |= 4ull << 61;            // layout: SWIZZLE_64B
+    return d;
+}
+
 __device__ __forceinline__ uint32_t elect_lane0() { return (threadIdx.x & 31) == 0; }
 
 }  // namespace pn

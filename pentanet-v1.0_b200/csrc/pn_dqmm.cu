@@ -82,7 +82,16 @@ struct Cfg {
     static constexpr bool kPerm = KIND == Kind::F16 && BT <= 64;
     static constexpr int kIssuers = BT <= 32 ? 4 : (BT <= 64 ? 2 : 1);
     static constexpr int kSlabBytes = BT * 32;
-    static constexpr int kXStageBytes = kSlabBytes * T::kSteps;
+    // Activation stage: the k-block's BT rows x kRowBytes.  Staged by TMA as
+    // kWide boxes of 128-byte rows (128-byte swizzle) and one box of the
+    // remaining kTail bytes per row (32- or 64-byte swizzle), each box BT rows;
+    // the MMA for K-step j reads bytes [32j, 32j + 32) of every row.  Bulk-copied
+    // decode stages are kSteps 32-byte-swizzled slabs instead.
+    static constexpr int kRowBytes = kKB * T::kXElem;
+    static constexpr int kWide = kRowBytes / 128;
+    static constexpr int kTail = kRowBytes % 128;
+    static constexpr int kXDataBytes = kSlabBytes * T::kSteps;
+    static constexpr int kXStageBytes = (kXDataBytes + 1023) / 1024 * 1024;
     static constexpr int kChunksPerRow = kKB * T::kXElem / 16;      // 16-byte pieces of one row per k-block
     static constexpr int kDCols = kIssuers * BT;                  // accumulators D_0..D_{kIssuers-1}
     static constexpr int kA0 = kDCols < 32 ? 32 : kDCols;         // first A column
@@ -114,6 +123,7 @@ struct Cfg {
     static_assert((kSX * kXStageBytes) % 1024 == 0, "weight stages must stay 1024-byte aligned (128B swizzle)");
     static_assert(kA0 + kSA * kAStageCols <= kTmemCols, "TMEM over-subscribed");
     static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "token tile");
+    static_assert(kTail == 32 || kTail == 64, "activation tail box");
 };
 
 struct DqmmParams {
@@ -131,7 +141,6 @@ struct DqmmParams {
     int acc_cols;          // columns of a 16-token tile's sum buffer: min(16, M)
     int* counters;         // [n_items][16 unpack warps] arrival counters of split tiles (zeroed by the host)
     int w_pad;      // weights read from a 16-byte-pitch copy in the workspace (unused by the kernel)
-    int x_mode;     // activation staging: 0 one 3D TMA box per k-block, 1 one 2D box per MMA K-step
     const uint8_t* xperm;  // permuted activation slabs (bf16 decode tiles)
     int64_t packed_bytes;
     float scale;
@@ -286,8 +295,8 @@ __device__ __forceinline__ void red_add(int* p, int v) {
 
 template <Kind KIND, int BT>
 __global__ void __launch_bounds__(kThreads, 1)
-    dqmm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
-                const DqmmParams p) {
+    dqmm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmap_tail,
+                const __grid_constant__ CUtensorMap wmap, const DqmmParams p) {
     using C = Cfg<KIND, BT>;
     using T = typename C::T;
     extern __shared__ uint8_t smem_raw[];
@@ -334,7 +343,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_relinquish();
     }
     if ((warp == kLoadWarp || warp == kLoadWarp2) && lane == 0) tma_prefetch_desc(&wmap);
-    if (warp == kXLoadWarp && lane == 0 && p.x_mode != 2) tma_prefetch_desc(&xmap);
+    if (warp == kXLoadWarp && lane == 0 && !C::kPerm) {
+        tma_prefetch_desc(&xmap);
+        tma_prefetch_desc(&xmap_tail);
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -385,17 +397,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!warp_wait(&empty_x[sx], ((it / C::kSX) & 1) ^ 1, abort_flag)) { ok = false; break; }
                 uint8_t* xs = smem_x + sx * C::kXStageBytes;
                 if (lane == 0) {
-                    mbar_arrive_expect_tx(&full_x[sx], C::kXStageBytes);
+                    mbar_arrive_expect_tx(&full_x[sx], C::kXDataBytes);
                     if constexpr (C::kPerm) {
-                        bulk_load(xs, p.xperm + (size_t)kb * C::kXStageBytes, C::kXStageBytes, &full_x[sx]);
-                    } else if (p.x_mode == 0) {
-                        // [slab][row][32 bytes] in one box
-                        tma_load_3d(xs, &xmap, &full_x[sx], 0, m0, kb * T::kSteps);
+                        bulk_load(xs, p.xperm + (size_t)kb * C::kXDataBytes, C::kXDataBytes, &full_x[sx]);
                     } else {
+                        const int k0 = kb * kKB;
 #pragma unroll
-                        for (int j = 0; j < T::kSteps; ++j)
-                            tma_load_2d(xs + j * C::kSlabBytes, &xmap, &full_x[sx],
-                                        (kb * T::kSteps + j) * T::kSlabElems, m0);
+                        for (int b = 0; b < C::kWide; ++b)
+                            tma_load_2d(xs + b * BT * 128, &xmap, &full_x[sx], k0 + b * (128 / T::kXElem), m0);
+                        tma_load_2d(xs + C::kWide * BT * 128, &xmap_tail, &full_x[sx],
+                                    k0 + C::kWide * (128 / T::kXElem), m0);
                     }
                 }
                 __syncwarp();
@@ -445,7 +456,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint32_t a_col = tmem_base + C::kA0 + sa * C::kAStageCols;
 #pragma unroll
                         for (int j = 0; j < C::kStepsPerA; ++j) {
-                            const uint64_t bdesc = smem_desc_sw32(xs + (hh * C::kStepsPerA + j) * C::kSlabBytes);
+                            const int step = hh * C::kStepsPerA + j;
+                            uint64_t bdesc;
+                            if constexpr (C::kPerm) {
+                                bdesc = smem_desc_sw32(xs + step * C::kSlabBytes);
+                            } else if (step * 32 < C::kWide * 128) {
+                                // inside a 128-byte-swizzled box: advance the start by 32 bytes per step
+                                bdesc = smem_desc_sw128(xs + (step * 32 / 128) * BT * 128 + (step * 32) % 128);
+                            } else if constexpr (C::kTail == 32) {
+                                bdesc = smem_desc_sw32(xs + C::kWide * BT * 128);
+                            } else {
+                                bdesc = smem_desc_sw64(xs + C::kWide * BT * 128 + (step * 32 - C::kWide * 128));
+                            }
                             const uint32_t acc = (first && j == 0) ? 0u : 1u;
                             if constexpr (KIND == Kind::F16)
                                 mma_f16_ts_warp(d_tmem, a_col + j * 8, bdesc, idesc, acc);
@@ -950,32 +972,25 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     const int64_t pitch_bytes = a.x_pitch * T::kXElem;
     const CUtensorMapDataType xdt = KIND == Kind::F16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
     cuuint32_t estr[3] = {1, 1, 1};
-    // Activations.  Preferred: one 3D box per k-block, viewing the rows as
-    // [slab][row][32 bytes] (slab = one MMA K-step), which needs whole slabs
-    // inside the row pitch.  Otherwise one 2D box per slab; columns >= K and
-    // rows >= M are zero-filled either way.
-    CUtensorMap xmap;
+    // Activations: two 2D maps over the (M, K) rows, one with a box of 128-byte
+    // rows (128-byte swizzle) and one with a box of the k-block's remaining
+    // 32 or 64 bytes per row (matching swizzle).  Columns >= K and rows >= M
+    // are zero-filled.  Decode tiles stage pre-arranged slabs without a map.
+    CUtensorMap xmap, xmap_tail;
     std::memset(&xmap, 0, sizeof(xmap));
-    int x_mode = 1;
-    const int64_t row_bytes = KIND == Kind::F16 ? a.K * 2 : pitch_bytes;  // bytes the kernel may read per row
-    if (C::kPerm) {
-        x_mode = 2;  // pre-arranged slabs, no tensor map
-    } else if (row_bytes % 32 == 0) {
-        cuuint64_t dims[3] = {(cuuint64_t)T::kSlabElems, (cuuint64_t)a.M, (cuuint64_t)(row_bytes / 32)};
-        cuuint64_t strides[2] = {(cuuint64_t)pitch_bytes, 32};
-        cuuint32_t box[3] = {(cuuint32_t)T::kSlabElems, (cuuint32_t)BT, (cuuint32_t)T::kSteps};
-        if (encode(&xmap, xdt, 3, const_cast<void*>(a.x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
-            x_mode = 0;
-    }
-    if (x_mode == 1) {
+    std::memset(&xmap_tail, 0, sizeof(xmap_tail));
+    if (!C::kPerm) {
         cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
         cuuint64_t strides[1] = {(cuuint64_t)pitch_bytes};
-        cuuint32_t box[2] = {(cuuint32_t)T::kSlabElems, (cuuint32_t)BT};
+        cuuint32_t box[2] = {(cuuint32_t)(128 / T::kXElem), (cuuint32_t)BT};
+        cuuint32_t box_tail[2] = {(cuuint32_t)(C::kTail / T::kXElem), (cuuint32_t)BT};
         if (encode(&xmap, xdt, 2, const_cast<void*>(a.x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+            encode(&xmap_tail, xdt, 2, const_cast<void*>(a.x), dims, strides, box_tail, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   C::kTail == 32 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
             *why = "cuTensorMapEncodeTiled rejected the activation layout";
             return PN_ERR_ALIGN;
         }
@@ -1033,7 +1048,6 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     prm.counters = reinterpret_cast<int*>(ws + L.counters);
     prm.n_kb = n_kblocks(a.KP);
     prm.w_pad = repitch;
-    prm.x_mode = x_mode;
     prm.packed_bytes = a.N * a.KP * 4;
     prm.xperm = ws + L.xperm;
     // split-tile counters start at zero (the decode pre-pass zeroes them, else a memset)
@@ -1100,9 +1114,9 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, kern, xmap, wmap, prm);
+        e = cudaLaunchKernelEx(&cfg, kern, xmap, xmap_tail, wmap, prm);
     } else {
-        kern<<<grid, kThreads, C::kSmem, s>>>(xmap, wmap, prm);
+        kern<<<grid, kThreads, C::kSmem, s>>>(xmap, xmap_tail, wmap, prm);
         e = cudaGetLastError();
     }
     if (e != cudaSuccess) {
