@@ -134,9 +134,11 @@ struct DqmmParams {
     int64_t total_pairs;   // n_items * (n_kb / 2): the flattened (tile, k-block pair) work
     int unit;              // pairs per indivisible unit: 1 (tiles may split) or n_kb / 2 (whole tiles)
     // Split tiles.  16-token tiles: one sum buffer per split tile,
-    // [gridDim.x][128][acc_cols] int64 fixed point (bf16 path) / int32,
+    // [gridDim.x][acc_cols][128] int64 fixed point (bf16 path) / int32,
     // added with atomics.  Larger tiles: per-CTA partials
-    // [gridDim.x][2][128][BT], summed by the last contributor.
+    // [gridDim.x][2][BT/4][128][4] (groups of 4 columns, row-major inside a
+    // group, so a warp's 16-byte accesses are contiguous), summed by the
+    // last contributor.
     void* accbuf;
     int acc_cols;          // columns of a 16-token tile's sum buffer: min(16, M)
     int* counters;         // [n_items][16 unpack warps] arrival counters of split tiles (zeroed by the host)
@@ -691,9 +693,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr bool kRedSum = BT <= 16;
             const int Pp = p.n_kb / 2;
             const int c_first = g.whole ? 0 : owner_of(p, (int64_t)g.tile * Pp);
-            const size_t acc_base = ((size_t)c_first * kRows + row) * p.acc_cols;
+            // sum (row, c) of the split tile at acc_base + c * kRows: a warp's lanes are contiguous
+            const size_t acc_base = (size_t)c_first * kRows * p.acc_cols + row;
             const int slot = g.tile == my_first_tile ? 0 : 1;
-            uint32_t* part = static_cast<uint32_t*>(p.accbuf) + ((size_t)(blockIdx.x * 2 + slot) * kRows + row) * BT;
+            // partial (row, c) at part[(c / 4) * 512 + c % 4]
+            uint32_t* part = static_cast<uint32_t*>(p.accbuf) + (size_t)(blockIdx.x * 2 + slot) * kRows * BT + row * 4;
             // This thread's accumulator columns: chunks c0 = 16*half + 64*i.
 #pragma unroll 1
             for (int c0 = 16 * half; c0 < BT; c0 += 16 * kUnpackGroups) {
@@ -715,15 +719,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < 16; ++j) {
                         if (m0 + c0 + j >= p.M) break;
                         if constexpr (KIND == Kind::F16)
-                            red_add(static_cast<long long*>(p.accbuf) + acc_base + c0 + j,
+                            red_add(static_cast<long long*>(p.accbuf) + acc_base + (size_t)(c0 + j) * kRows,
                                     __float2ll_rn(__uint_as_float(acc[j]) * kFixScale));
                         else
-                            red_add(static_cast<int*>(p.accbuf) + acc_base + c0 + j, (int)acc[j]);
+                            red_add(static_cast<int*>(p.accbuf) + acc_base + (size_t)(c0 + j) * kRows, (int)acc[j]);
                     }
                 } else {
 #pragma unroll
                     for (int j = 0; j < 16; j += 4)
-                        *reinterpret_cast<uint4*>(part + c0 + j) = make_uint4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+                        *reinterpret_cast<uint4*>(part + (c0 + j) * kRows) =
+                            make_uint4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
                 }
             }
             // TMEM is free for the next segment.
@@ -759,10 +764,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 if (m0 + c0 + j < p.M) {
                                     if constexpr (KIND == Kind::F16) {
                                         const long long v =
-                                            __ldcg(static_cast<const long long*>(p.accbuf) + acc_base + c0 + j);
+                                            __ldcg(static_cast<const long long*>(p.accbuf) + acc_base + (size_t)(c0 + j) * kRows);
                                         acc[j] = __float_as_uint(__ll2float_rn(v) * (1.0f / kFixScale));
                                     } else {
-                                        acc[j] = (uint32_t)__ldcg(static_cast<const int*>(p.accbuf) + acc_base + c0 + j);
+                                        acc[j] = (uint32_t)__ldcg(static_cast<const int*>(p.accbuf) + acc_base + (size_t)(c0 + j) * kRows);
                                     }
                                 }
                             }
@@ -772,10 +777,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                             for (int c = c_first; c <= c_last; ++c) {
                                 const int slot_c = g.tile == (int)(range_begin(p, c) / Pp) ? 0 : 1;
                                 const uint32_t* pc = static_cast<const uint32_t*>(p.accbuf) +
-                                                     ((size_t)(c * 2 + slot_c) * kRows + row) * BT + c0;
+                                                     (size_t)(c * 2 + slot_c) * kRows * BT + row * 4 + c0 * kRows;
 #pragma unroll
                                 for (int j = 0; j < 16; j += 4) {
-                                    const uint4 q4 = __ldcg(reinterpret_cast<const uint4*>(pc + j));
+                                    const uint4 q4 = __ldcg(reinterpret_cast<const uint4*>(pc + j * kRows));
                                     if (c == c_first) {
                                         acc[j] = q4.x;
                                         acc[j + 1] = q4.y;
