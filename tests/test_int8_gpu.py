@@ -112,3 +112,24 @@ def test_int8_split_and_whole_tile_schedules(cuda_device, M, N, K):
                             ws.data_ptr(), nbytes, nat.stream_of(xq))
         assert st == nat.PN_OK, L.pn_last_error()
         assert np.array_equal(acc.cpu().numpy(), want), f"workspace {nbytes}"
+
+
+@pytest.mark.parametrize("K", [8, 16, 96, 768, 1000, 2048, 3072, 4096, 8192, 11008, 28672, 40000])
+@pytest.mark.parametrize("M", [1, 7, 33])
+def test_quantiser_all_row_lengths(cuda_device, M, K):
+    """Every threads-per-token variant of the vectorised quantiser (rows of 8
+    to 32768), the scalar kernel (K % 8 != 0, longer rows) and exact
+    half-integer quotients (rounded half to even, as the reference's division
+    then round)."""
+    x = gen_act(M, K, seed=M * 7 + K)
+    x[0, :4] = torch.tensor([3.0, -7.5, 4.5, 0.5])   # with s = 3: x / s = 1, -2.5, 1.5, 1/6
+    x[0, 4] = 381.0                                   # s = 3 exactly
+    if M > 1:
+        x[1] = 0                                      # all-zero row: s = 1
+    x = x.to(torch.bfloat16)
+    xq, s_x, rowsum = pk.quantize_activations_i8(x.to(cuda_device))
+    want_q, want_s = orc.quant_act_i8(x.float().numpy())
+    assert np.array_equal(xq[:, :K].cpu().numpy(), want_q)
+    assert not xq[:, K:].any()
+    assert np.array_equal(s_x.cpu().numpy(), want_s)
+    assert np.array_equal(rowsum.cpu().numpy(), want_q.astype(np.int64).sum(1))
