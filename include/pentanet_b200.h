@@ -104,6 +104,21 @@ int pn_linear_bf16(const void *x, int64_t M, int64_t K, const int32_t *packed, i
                    float scale, const void *bias, void *y, int y_dtype, void *workspace,
                    size_t workspace_bytes, void *stream);
 
+/* pn_linear_bf16 with the packed rows packed_ld int32 words apart
+ * (packed_ld >= K_packs; the (N, K_packs) tensor may be a view of a wider
+ * buffer).  With packed_ld % 4 == 0 the rows are 16 bytes apart and are read
+ * in place; pn_linear_bf16 (packed_ld = K_packs) otherwise copies them into the
+ * workspace at a 16-byte pitch on every call, so callers that keep weights
+ * resident store them at pn_packed_ld(K_packs).  Replaces penta_linear
+ * (penta_kernel.py:229-278) for such stored weights. */
+int pn_linear_bf16_ld(const void *x, int64_t M, int64_t K, const int32_t *packed, int64_t N, int64_t K_packs,
+                      int64_t packed_ld, float scale, const void *bias, void *y, int y_dtype, void *workspace,
+                      size_t workspace_bytes, void *stream);
+
+/* The packed row stride (int32 words) that lets the GEMM read weights in
+ * place: K_packs rounded up to a multiple of 4. */
+int64_t pn_packed_ld(int64_t K_packs);
+
 /* pn_linear_bf16 without a workspace argument, for callers that cannot
  * allocate device memory (code where no allocator may run, or embeddings that
  * hand the library only raw input/output pointers).  No counterpart in the
@@ -137,6 +152,13 @@ int pn_linear_i8(const int8_t *xq, int64_t xq_pitch, const float *s_x, const int
                  int64_t K, const int32_t *packed, int64_t N, int64_t K_packs, float scale, const void *bias,
                  void *y, int y_dtype, int32_t *acc_out, void *workspace, size_t workspace_bytes,
                  void *stream);
+
+/* pn_linear_i8 with the packed rows packed_ld int32 words apart (as
+ * pn_linear_bf16_ld). */
+int pn_linear_i8_ld(const int8_t *xq, int64_t xq_pitch, const float *s_x, const int32_t *rowsum, int64_t M,
+                    int64_t K, const int32_t *packed, int64_t N, int64_t K_packs, int64_t packed_ld, float scale,
+                    const void *bias, void *y, int y_dtype, int32_t *acc_out, void *workspace,
+                    size_t workspace_bytes, void *stream);
 
 /* Number of SMs of the current device (used to size launches and shards). */
 int pn_device_sm_count(int *count_out);

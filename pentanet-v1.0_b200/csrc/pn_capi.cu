@@ -154,9 +154,9 @@ size_t pn_linear_workspace_min_size(int kind, int64_t M, int64_t N, int64_t K) {
 namespace {
 // pn_linear_bf16 and its output-sharded form share validation and launch.
 int linear_bf16_impl(const void* x, int64_t M, int64_t K, const int32_t* packed, int64_t N, int64_t K_packs,
-                     float scale, const void* bias, void* y, int y_dtype, void* workspace, size_t workspace_bytes,
-                     void* stream, void* const* y_peers, int n_peers, int64_t ld_y, int64_t y_col0,
-                     const char* name) {
+                     int64_t packed_ld, float scale, const void* bias, void* y, int y_dtype, void* workspace,
+                     size_t workspace_bytes, void* stream, void* const* y_peers, int n_peers, int64_t ld_y,
+                     int64_t y_col0, const char* name) {
     if ((!x && M > 0) || (!packed && N > 0) || (!y && n_peers == 0 && M > 0 && N > 0))
         return fail(PN_ERR_ARG, "%s: null pointer", name);
     if (y_dtype != PN_BF16 && y_dtype != PN_F32) return fail(PN_ERR_DTYPE, "%s: y_dtype %d", name, y_dtype);
@@ -165,6 +165,8 @@ int linear_bf16_impl(const void* x, int64_t M, int64_t K, const int32_t* packed,
     if (K_packs != k_packs(K))
         return fail(PN_ERR_SHAPE, "%s: activation K=%lld needs K_packs=%lld, got %lld", name, (long long)K,
                     (long long)k_packs(K), (long long)K_packs);
+    if (packed_ld < K_packs)
+        return fail(PN_ERR_SHAPE, "%s: packed_ld=%lld < K_packs=%lld", name, (long long)packed_ld, (long long)K_packs);
     if (!aligned(x, 2) || !aligned(packed, 16) || !aligned(y, y_dtype == PN_F32 ? 4 : 2) || !aligned(bias, 2))
         return fail(PN_ERR_ALIGN, "%s: misaligned pointer (packed weights need 16-byte alignment)", name);
     const size_t need = pn::linear_workspace_min_bytes(PN_BF16, M, N, K);
@@ -182,6 +184,7 @@ int linear_bf16_impl(const void* x, int64_t M, int64_t K, const int32_t* packed,
     a.N = N;
     a.KP = K_packs;
     a.packed = packed;
+    a.packed_ld = packed_ld;
     a.scale = scale;
     a.bias = bias;
     a.y = y;
@@ -212,8 +215,17 @@ extern "C" {
 int pn_linear_bf16(const void* x, int64_t M, int64_t K, const int32_t* packed, int64_t N, int64_t K_packs,
                    float scale, const void* bias, void* y, int y_dtype, void* workspace, size_t workspace_bytes,
                    void* stream) {
-    return linear_bf16_impl(x, M, K, packed, N, K_packs, scale, bias, y, y_dtype, workspace, workspace_bytes, stream,
-                            nullptr, 0, 0, 0, "pn_linear_bf16");
+    return linear_bf16_impl(x, M, K, packed, N, K_packs, K_packs, scale, bias, y, y_dtype, workspace, workspace_bytes,
+                            stream, nullptr, 0, 0, 0, "pn_linear_bf16");
+}
+
+int64_t pn_packed_ld(int64_t K_packs) { return K_packs <= 0 ? 0 : (K_packs + 3) / 4 * 4; }
+
+int pn_linear_bf16_ld(const void* x, int64_t M, int64_t K, const int32_t* packed, int64_t N, int64_t K_packs,
+                      int64_t packed_ld, float scale, const void* bias, void* y, int y_dtype, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+    return linear_bf16_impl(x, M, K, packed, N, K_packs, packed_ld, scale, bias, y, y_dtype, workspace,
+                            workspace_bytes, stream, nullptr, 0, 0, 0, "pn_linear_bf16_ld");
 }
 
 int64_t pn_act_i8_pitch(int64_t K) { return pn::act_i8_pitch(K); }
@@ -232,9 +244,10 @@ int pn_quant_act_i8(const void* x, int x_dtype, int64_t M, int64_t K, int8_t* xq
     return e == cudaSuccess ? ok() : cuda_fail(e, "pn_quant_act_i8");
 }
 
-int pn_linear_i8(const int8_t* xq, int64_t xq_pitch, const float* s_x, const int32_t* rowsum, int64_t M, int64_t K,
-                 const int32_t* packed, int64_t N, int64_t K_packs, float scale, const void* bias, void* y,
-                 int y_dtype, int32_t* acc_out, void* workspace, size_t workspace_bytes, void* stream) {
+static int linear_i8_impl(const int8_t* xq, int64_t xq_pitch, const float* s_x, const int32_t* rowsum, int64_t M,
+                          int64_t K, const int32_t* packed, int64_t N, int64_t K_packs, int64_t packed_ld, float scale,
+                          const void* bias, void* y, int y_dtype, int32_t* acc_out, void* workspace,
+                          size_t workspace_bytes, void* stream) {
     if (M > 0 && N > 0 && (!xq || !s_x || !rowsum || !packed || (!y && !acc_out)))
         return fail(PN_ERR_ARG, "pn_linear_i8: null pointer");
     if (y && y_dtype != PN_BF16 && y_dtype != PN_F32) return fail(PN_ERR_DTYPE, "pn_linear_i8: y_dtype %d", y_dtype);
@@ -244,6 +257,9 @@ int pn_linear_i8(const int8_t* xq, int64_t xq_pitch, const float* s_x, const int
     if (K_packs != k_packs(K))
         return fail(PN_ERR_SHAPE, "pn_linear_i8: K=%lld needs K_packs=%lld, got %lld", (long long)K,
                     (long long)k_packs(K), (long long)K_packs);
+    if (packed_ld < K_packs)
+        return fail(PN_ERR_SHAPE, "pn_linear_i8: packed_ld=%lld < K_packs=%lld", (long long)packed_ld,
+                    (long long)K_packs);
     if (!aligned(xq, 16) || !aligned(packed, 16) || !aligned(s_x, 4) || !aligned(rowsum, 4) || !aligned(acc_out, 4) ||
         !aligned(y, y_dtype == PN_F32 ? 4 : 2) || !aligned(bias, 2))
         return fail(PN_ERR_ALIGN, "pn_linear_i8: misaligned pointer");
@@ -262,6 +278,7 @@ int pn_linear_i8(const int8_t* xq, int64_t xq_pitch, const float* s_x, const int
     a.N = N;
     a.KP = K_packs;
     a.packed = packed;
+    a.packed_ld = packed_ld;
     a.scale = scale;
     a.bias = bias;
     a.y = y;
@@ -277,6 +294,21 @@ int pn_linear_i8(const int8_t* xq, int64_t xq_pitch, const float* s_x, const int
     if (st == PN_ERR_CUDA) return cuda_fail(ce, why);
     if (st != PN_OK) return fail(st, "pn_linear_i8: %s", why);
     return ok();
+}
+
+int pn_linear_i8(const int8_t* xq, int64_t xq_pitch, const float* s_x, const int32_t* rowsum, int64_t M, int64_t K,
+                 const int32_t* packed, int64_t N, int64_t K_packs, float scale, const void* bias, void* y,
+                 int y_dtype, int32_t* acc_out, void* workspace, size_t workspace_bytes, void* stream) {
+    return linear_i8_impl(xq, xq_pitch, s_x, rowsum, M, K, packed, N, K_packs, K_packs, scale, bias, y, y_dtype,
+                          acc_out, workspace, workspace_bytes, stream);
+}
+
+int pn_linear_i8_ld(const int8_t* xq, int64_t xq_pitch, const float* s_x, const int32_t* rowsum, int64_t M,
+                    int64_t K, const int32_t* packed, int64_t N, int64_t K_packs, int64_t packed_ld, float scale,
+                    const void* bias, void* y, int y_dtype, int32_t* acc_out, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+    return linear_i8_impl(xq, xq_pitch, s_x, rowsum, M, K, packed, N, K_packs, packed_ld, scale, bias, y, y_dtype,
+                          acc_out, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

@@ -127,7 +127,6 @@ struct Cfg {
 };
 
 struct DqmmParams {
-    const int32_t* packed;
     int64_t N, KP;
     int M;
     int n_row_tiles, n_items, n_kb;
@@ -142,9 +141,7 @@ struct DqmmParams {
     void* accbuf;
     int acc_cols;          // columns of a 16-token tile's sum buffer: min(16, M)
     int* counters;         // [n_items][16 unpack warps] arrival counters of split tiles (zeroed by the host)
-    int w_pad;      // weights read from a 16-byte-pitch copy in the workspace (unused by the kernel)
     const uint8_t* xperm;  // permuted activation slabs (bf16 decode tiles)
-    int64_t packed_bytes;
     float scale;
     const __nv_bfloat16* bias;
     void* y_out[8];        // output buffers (one, or one per GPU of an output-sharded layer)
@@ -955,13 +952,15 @@ size_t linear_workspace_min_bytes(int kind, int64_t M, int64_t N, int64_t K) {
     return ws_layout(kind, M, N, K, false).total;
 }
 
-// Copies packed rows into a 16-byte pitch so that TMA can address them.
-__global__ void __launch_bounds__(256) repitch_kernel(const int32_t* __restrict__ src, int64_t N, int64_t KP,
-                                                      int64_t pitch, int32_t* __restrict__ dst) {
+// Copies packed rows (src_ld words apart) into a 16-byte pitch so that TMA
+// can address them.
+__global__ void __launch_bounds__(256) repitch_kernel(const int32_t* __restrict__ src, int64_t src_ld, int64_t N,
+                                                      int64_t KP, int64_t pitch, int32_t* __restrict__ dst) {
     const int64_t total = N * KP;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t n = i / KP;
-        dst[n * pitch + (i - n * KP)] = __ldg(src + i);
+        const int64_t w = i - n * KP;
+        dst[n * pitch + w] = __ldg(src + n * src_ld + w);
     }
 }
 
@@ -1016,14 +1015,17 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
         return PN_ERR_WORKSPACE;
     }
     uint8_t* ws = static_cast<uint8_t*>(a.workspace);
-    const bool repitch = a.KP % 4 != 0;
-    const int64_t pitch = repitch ? w_pitch(a.KP) : a.KP;
+    // TMA reads the rows in place when they are 16 bytes apart (a multiple of
+    // 4 words: K_packs % 4 == 0, or rows stored at a padded stride); other
+    // layouts are first copied into the workspace at a 16-byte pitch.
+    const bool repitch = a.packed_ld % 4 != 0;
+    const int64_t pitch = repitch ? w_pitch(a.KP) : a.packed_ld;
     const int32_t* wsrc = a.packed;
     if (repitch) {
         int32_t* dst = reinterpret_cast<int32_t*>(ws + L.wpitch);
         const int64_t total = a.N * a.KP;
         const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
-        repitch_kernel<<<blocks, 256, 0, s>>>(a.packed, a.N, a.KP, pitch, dst);
+        repitch_kernel<<<blocks, 256, 0, s>>>(a.packed, a.packed_ld, a.N, a.KP, pitch, dst);
         wsrc = dst;
     }
     CUtensorMap wmap;
@@ -1039,7 +1041,6 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
         }
     }
     DqmmParams prm;
-    prm.packed = a.packed;
     prm.N = a.N;
     prm.KP = a.KP;
     prm.M = (int)a.M;
@@ -1052,8 +1053,6 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     prm.acc_cols = L.acc_cols;
     prm.counters = reinterpret_cast<int*>(ws + L.counters);
     prm.n_kb = n_kblocks(a.KP);
-    prm.w_pad = repitch;
-    prm.packed_bytes = a.N * a.KP * 4;
     prm.xperm = ws + L.xperm;
     // split-tile counters start at zero (the decode pre-pass zeroes them, else a memset)
     const int64_t n_zero16 = L.unit == 1 ? (int64_t)(L.zero_bytes / 16) : 0;

@@ -23,6 +23,7 @@ struct LinearArgs {
     int64_t x_pitch;          // elements per X row
     int64_t M, K, N, KP;
     const int32_t* packed;
+    int64_t packed_ld;        // int32 words between packed rows (>= KP)
     float scale;
     const void* bias;         // bf16 (N) or null
     void* y;                  // (M, N) or null (int8 path only)

@@ -12,13 +12,14 @@ constexpr int kSimtTok = 8;  // tokens per pass
 
 // One warp per weight row; lanes stride over the row's packed words.
 __global__ void __launch_bounds__(256) simt_bf16_kernel(const __nv_bfloat16* __restrict__ x, int64_t M, int64_t K,
-                                                        const int32_t* __restrict__ packed, int64_t N, int64_t KP,
+                                                        const int32_t* __restrict__ packed, int64_t ld, int64_t N,
+                                                        int64_t KP,
                                                         float scale, const __nv_bfloat16* __restrict__ bias,
                                                         void* __restrict__ y, int y_f32) {
     const int64_t n = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (n >= N) return;
-    const int32_t* prow = packed + n * KP;
+    const int32_t* prow = packed + n * ld;
     const float bias_f = bias ? __bfloat162float(bias[n]) : 0.0f;
     for (int64_t m0 = 0; m0 < M; m0 += kSimtTok) {
         float acc[kSimtTok];
@@ -62,7 +63,7 @@ cudaError_t launch_linear_simt_bf16(const LinearArgs& a, cudaStream_t s) {
     if (a.M == 0 || a.N == 0) return cudaSuccess;
     const int warps = 8;
     const unsigned blocks = (unsigned)((a.N + warps - 1) / warps);
-    simt_bf16_kernel<<<blocks, warps * 32, 0, s>>>(static_cast<const __nv_bfloat16*>(a.x), a.M, a.K, a.packed, a.N,
+    simt_bf16_kernel<<<blocks, warps * 32, 0, s>>>(static_cast<const __nv_bfloat16*>(a.x), a.M, a.K, a.packed, a.packed_ld, a.N,
                                                    a.KP, a.scale, static_cast<const __nv_bfloat16*>(a.bias), a.y,
                                                    a.y_dtype == PN_F32);
     return cudaGetLastError();

@@ -137,6 +137,40 @@ def storage_bytes(N: int, K: int) -> int:
     return 4 * N * _k_packs(K)
 
 
+# ── Resident weight layout ───────────────────────────────────────────────────
+
+def packed_ld(K_packs: int) -> int:
+    """Row stride (int32 words) at which the GEMM reads packed rows in place:
+    K_packs rounded up to a multiple of 4 (16-byte rows for TMA)."""
+    return (int(K_packs) + 3) // 4 * 4
+
+
+def pad_packed(packed: torch.Tensor) -> torch.Tensor:
+    """The same (N, K_packs) packed weights stored at row stride
+    packed_ld(K_packs): a view of a zero-padded (N, packed_ld) buffer.  Values
+    and shape are unchanged; penta_linear / penta_linear_i8 read such rows in
+    place instead of re-pitching the weights on every call (when K_packs is not
+    a multiple of 4).  Not in the reference; used for weights kept resident
+    (PentaLinearFast)."""
+    assert packed.dim() == 2 and packed.dtype == torch.int32
+    N, KP = packed.shape
+    ld = packed_ld(KP)
+    if packed.stride(1) == 1 and packed.stride(0) == ld:
+        return packed
+    buf = torch.zeros(N, ld, dtype=torch.int32, device=packed.device)
+    buf[:, :KP].copy_(packed)
+    return buf[:, :KP]
+
+
+def _packed_rows(packed_w: torch.Tensor) -> tuple[torch.Tensor, int]:
+    """(tensor, row stride in words) to hand to the C ABI: strided views with
+    unit column stride are passed as they are, anything else is made contiguous."""
+    if packed_w.dim() == 2 and packed_w.stride(1) == 1 and packed_w.stride(0) >= packed_w.shape[1]:
+        return packed_w, int(packed_w.stride(0))
+    pw = packed_w.contiguous()
+    return pw, int(pw.shape[1])
+
+
 # ── Fused dequant-matmul ─────────────────────────────────────────────────────
 
 def penta_linear(x: torch.Tensor, packed_w: torch.Tensor, scale: float, K_orig: int,
@@ -164,7 +198,7 @@ def penta_linear(x: torch.Tensor, packed_w: torch.Tensor, scale: float, K_orig: 
     M, K = x_2d.shape
     N, K_packs = packed_w.shape
     assert K == K_orig, f"Activation K={K} must match K_orig={K_orig}"
-    pw = packed_w.contiguous()
+    pw, ld = _packed_rows(packed_w)
     y = torch.empty(M, N, device=x.device, dtype=out_dtype)
     b = None
     if bias is not None:
@@ -173,10 +207,10 @@ def penta_linear(x: torch.Tensor, packed_w: torch.Tensor, scale: float, K_orig: 
     L = _nat.load()
     ws_bytes = int(L.pn_linear_workspace_size(_nat.PN_BF16, M, N, K))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
-    _nat.check(L.pn_linear_bf16(x_2d.data_ptr(), M, K, pw.data_ptr(), N, K_packs, ctypes.c_float(scale),
-                                _nat.ptr(b), y.data_ptr(),
-                                _nat.PN_F32 if out_dtype == torch.float32 else _nat.PN_BF16,
-                                _nat.ptr(ws), ws_bytes, _nat.stream_of(x_2d)), "penta_linear")
+    _nat.check(L.pn_linear_bf16_ld(x_2d.data_ptr(), M, K, pw.data_ptr(), N, K_packs, ld, ctypes.c_float(scale),
+                                   _nat.ptr(b), y.data_ptr(),
+                                   _nat.PN_F32 if out_dtype == torch.float32 else _nat.PN_BF16,
+                                   _nat.ptr(ws), ws_bytes, _nat.stream_of(x_2d)), "penta_linear")
     return y.reshape(*orig_shape[:-1], N)
 
 
@@ -212,7 +246,7 @@ def penta_linear_i8_prequant(xq: torch.Tensor, s_x: torch.Tensor, rowsum: torch.
     M, pitch = xq.shape
     N, K_packs = packed_w.shape
     assert K_packs == _k_packs(K_orig), "packed weights do not match K_orig"
-    pw = packed_w.contiguous()
+    pw, ld = _packed_rows(packed_w)
     y = torch.empty(M, N, device=xq.device, dtype=out_dtype) if out_dtype is not None else None
     acc = torch.empty(M, N, device=xq.device, dtype=torch.int32) if return_acc else None
     b = bias.detach().to(device=xq.device, dtype=torch.bfloat16).contiguous() if bias is not None else None
@@ -220,9 +254,9 @@ def penta_linear_i8_prequant(xq: torch.Tensor, s_x: torch.Tensor, rowsum: torch.
     ws_bytes = int(L.pn_linear_workspace_size(_nat.PN_I8, M, N, K_orig))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=xq.device) if ws_bytes else None
     ydt = _nat.PN_F32 if out_dtype == torch.float32 else _nat.PN_BF16
-    _nat.check(L.pn_linear_i8(xq.data_ptr(), pitch, s_x.data_ptr(), rowsum.data_ptr(), M, K_orig, pw.data_ptr(),
-                              N, K_packs, ctypes.c_float(scale), _nat.ptr(b), _nat.ptr(y), ydt, _nat.ptr(acc),
-                              _nat.ptr(ws), ws_bytes, _nat.stream_of(xq)), "penta_linear_i8")
+    _nat.check(L.pn_linear_i8_ld(xq.data_ptr(), pitch, s_x.data_ptr(), rowsum.data_ptr(), M, K_orig,
+                                 pw.data_ptr(), N, K_packs, ld, ctypes.c_float(scale), _nat.ptr(b), _nat.ptr(y), ydt,
+                                 _nat.ptr(acc), _nat.ptr(ws), ws_bytes, _nat.stream_of(xq)), "penta_linear_i8")
     return (y, acc) if return_acc else y
 
 

@@ -68,6 +68,7 @@ class PentaLinearFast(nn.Module):
         super().__init__()
         assert act_quant in (None, 'int8')
         self.register_buffer('packed_w', packed_w)  # (N, K_packs) int32
+        self._pad_weights()
         self.scale = float(scale)
         self.K_orig = int(K_orig)
         self.act_quant = act_quant
@@ -86,6 +87,18 @@ class PentaLinearFast(nn.Module):
         packed, K_orig, scale = quantize_and_pack(layer.weight.detach())
         bias = layer.bias.detach().clone() if getattr(layer, 'bias', None) is not None else None
         return cls(packed, scale, K_orig, bias, act_quant=act_quant)
+
+    def _pad_weights(self) -> None:
+        # Resident CUDA weights are kept at a 16-byte row stride (same shape and
+        # values; see penta_kernel.pad_packed) so that the GEMM reads them in
+        # place instead of re-pitching them on every call.
+        if self.packed_w.is_cuda:
+            self.packed_w = _pk.pad_packed(self.packed_w)
+
+    def _apply(self, fn, *args, **kwargs):
+        super()._apply(fn, *args, **kwargs)  # device moves copy buffers contiguously
+        self._pad_weights()
+        return self
 
     def _load_from_state_dict(self, state_dict, prefix, *args, **kwargs):
         super()._load_from_state_dict(state_dict, prefix, *args, **kwargs)

@@ -83,6 +83,11 @@ def test_state_dict_keeps_scale_and_k(cuda_device):
     x = torch.randn(3, 96, device=cuda_device)
     assert torch.equal(clone(x), fast(x))
     assert "in=96, out=40" in repr(fast)
+    # resident weights sit at a 16-byte row stride (K_packs = 10 -> 12 words),
+    # also after a device round trip
+    assert fast.packed_w.shape == (40, 10) and fast.packed_w.stride(0) == 12
+    moved = fast.cpu().to(cuda_device)
+    assert moved.packed_w.stride(0) == 12 and torch.equal(moved(x), clone(x))
 
 
 def test_int8_activation_mode(cuda_device):

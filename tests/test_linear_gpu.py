@@ -206,3 +206,25 @@ def test_split_and_whole_tile_schedules(cuda_device, M, N, K):
                                   y.data_ptr(), nat.PN_F32, ws.data_ptr(), least - 1, nat.stream_of(x))
             assert st == nat.PN_ERR_WORKSPACE
     assert nat.device_status(reset=True) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 300, 770), (16, 256, 4096), (200, 384, 1001), (300, 256, 4096)])
+def test_padded_row_stride(cuda_device, M, N, K):
+    """Weights stored at a 16-byte row stride (pad_packed, the resident layout
+    of PentaLinearFast) give the same bits as the contiguous tensor, which is
+    re-pitched per call; any other stride is accepted too."""
+    packed, gamma, w8 = _layer(N, K, seed=M + N, dev=cuda_device)
+    x = gen_act(M, K, seed=K + 1).to(torch.bfloat16).to(cuda_device)
+    padded = pk.pad_packed(packed)
+    assert padded.shape == packed.shape and torch.equal(padded, packed)
+    assert padded.stride(0) == pk.packed_ld(packed.shape[1]) and padded.stride(0) % 4 == 0
+    assert pk.pad_packed(padded) is padded
+    wide = torch.zeros(N, packed.shape[1] + 5, dtype=torch.int32, device=cuda_device)
+    wide[:, :packed.shape[1]] = packed
+    ref = pk.penta_linear(x, packed, gamma, K, out_dtype=torch.float32)
+    for pw in (padded, wide[:, :packed.shape[1]]):
+        assert torch.equal(pk.penta_linear(x, pw, gamma, K, out_dtype=torch.float32), ref)
+        y8, acc8 = pk.penta_linear_i8(x, pw, gamma, K, out_dtype=torch.float32, return_acc=True)
+        y8c, acc8c = pk.penta_linear_i8(x, packed, gamma, K, out_dtype=torch.float32, return_acc=True)
+        assert torch.equal(acc8, acc8c) and torch.equal(y8, y8c)
+    _check(x, padded, gamma, w8, K, what="padded")
