@@ -104,6 +104,7 @@ struct Cfg {
     // one), so that an unpack group fills one stage while the MMAs read its other.
     static constexpr int kAStageCols = T::kACols / T::kAPerKB;
     static constexpr int kStepsPerA = T::kSteps / T::kAPerKB;
+    static_assert(kStepsPerA == 5, "five MMAs per operand stage");
     static constexpr int kAParties = kUnpackGroups * T::kAPerKB;  // stage uses per round of groups
     static constexpr int kSAfit = (kTmemCols - kA0) / kAStageCols;
     static constexpr int kSA = (kSAfit >= 8 ? 8 : kSAfit) / kAParties * kAParties;
@@ -445,7 +446,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t ik = it0 + j;
                     const int sx = ik % C::kSX;
                     if (!warp_wait(&full_x[sx], (ik / C::kSX) & 1, abort_flag)) { ok = false; break; }
-                    const uint8_t* xs = smem_x + sx * C::kXStageBytes;
+                    // descriptor low word of the stage: start address >> 4, leading offset 1
+                    const uint32_t xs_lo = (smem_u32(smem_x + sx * C::kXStageBytes) >> 4) + (1u << 16);
 #pragma unroll
                     for (int hh = 0; hh < T::kAPerKB; ++hh) {
                         const uint32_t ua = ik * T::kAPerKB + hh;  // operand stage use
@@ -453,26 +455,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (!warp_wait(&full_a[sa], (ua / C::kSA) & 1, abort_flag)) { ok = false; break; }
                         tc_fence_after();
                         const uint32_t a_col = tmem_base + C::kA0 + sa * C::kAStageCols;
+                        uint32_t lo[5], hi[5];
 #pragma unroll
-                        for (int j = 0; j < C::kStepsPerA; ++j) {
+                        for (int j = 0; j < 5; ++j) {
                             const int step = hh * C::kStepsPerA + j;
-                            uint64_t bdesc;
                             if constexpr (C::kPerm) {
-                                bdesc = smem_desc_sw32(xs + step * C::kSlabBytes);
+                                lo[j] = xs_lo + ((step * C::kSlabBytes) >> 4);
+                                hi[j] = kDescHiSW32;
                             } else if (step * 32 < C::kWide * 128) {
-                                // inside a 128-byte-swizzled box: advance the start by 32 bytes per step
-                                bdesc = smem_desc_sw128(xs + (step * 32 / 128) * BT * 128 + (step * 32) % 128);
+                                // inside a 128-byte-swizzled box: the start advances 32 bytes per step
+                                lo[j] = xs_lo + (((step * 32 / 128) * BT * 128 + (step * 32) % 128) >> 4);
+                                hi[j] = kDescHiSW128;
                             } else if constexpr (C::kTail == 32) {
-                                bdesc = smem_desc_sw32(xs + C::kWide * BT * 128);
+                                lo[j] = xs_lo + ((C::kWide * BT * 128) >> 4);
+                                hi[j] = kDescHiSW32;
                             } else {
-                                bdesc = smem_desc_sw64(xs + C::kWide * BT * 128 + (step * 32 - C::kWide * 128));
+                                lo[j] = xs_lo + ((C::kWide * BT * 128 + (step * 32 - C::kWide * 128)) >> 4);
+                                hi[j] = kDescHiSW64;
                             }
-                            const uint32_t acc = (first && j == 0) ? 0u : 1u;
-                            if constexpr (KIND == Kind::F16)
-                                mma_f16_ts_warp(d_tmem, a_col + j * 8, bdesc, idesc, acc);
-                            else
-                                mma_i8_ts_warp(d_tmem, a_col + j * 8, bdesc, idesc, acc);
                         }
+                        mma5_ts_warp<KIND == Kind::I8>(d_tmem, a_col, lo, hi, idesc, first ? 0u : 1u);
                         first = false;
                     }
                     if (!ok) break;

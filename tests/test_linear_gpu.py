@@ -228,3 +228,15 @@ def test_padded_row_stride(cuda_device, M, N, K):
         y8c, acc8c = pk.penta_linear_i8(x, packed, gamma, K, out_dtype=torch.float32, return_acc=True)
         assert torch.equal(acc8, acc8c) and torch.equal(y8, y8c)
     _check(x, padded, gamma, w8, K, what="padded")
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 200, 10), (2, 300, 170), (5, 256, 1600), (8, 384, 8192), (1, 640, 28672),
+                                   (3, 130, 31999), (8, 128, 9984)])
+def test_resident_activation_decode(cuda_device, M, N, K):
+    """Decode products of at most 8 tokens whose activations fit in shared
+    memory keep them resident for the launch (compact unswizzled image); the
+    larger shapes here fall back to the streamed slabs."""
+    packed, gamma, w8 = _layer(N, K, seed=K + M, dev=cuda_device)
+    x = gen_act(M, K, seed=N + 3).to(torch.bfloat16).to(cuda_device)
+    _check(x, packed, gamma, w8, K, what=f"resident M={M} K={K}")
+    _check(x, pk.pad_packed(packed), gamma, w8, K, what=f"resident padded M={M} K={K}")
