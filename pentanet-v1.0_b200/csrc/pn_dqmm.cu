@@ -132,6 +132,7 @@ struct DqmmParams {
     int M;
     int n_row_tiles, n_items, n_kb;
     int64_t total_pairs;   // n_items * (n_kb / 2): the flattened (tile, k-block pair) work
+    uint32_t units;        // total_pairs / unit
     int unit;              // pairs per indivisible unit: 1 (tiles may split) or n_kb / 2 (whole tiles)
     // Split tiles.  16-token tiles: one sum buffer per split tile,
     // [gridDim.x][acc_cols][128] int64 fixed point (bf16 path) / int32,
@@ -258,19 +259,22 @@ struct Seg {
     int kb0, kb1;   // k-blocks [kb0, kb1), both even
     bool whole;
 };
+// All in 32-bit unsigned arithmetic (the host checks that units * (grid + 1)
+// fits): these run at the start of every role and segment, and 64-bit
+// divisions cost hundreds of cycles there.
 __device__ __forceinline__ int64_t range_begin(const DqmmParams& p, int c) {
-    const int64_t units = p.total_pairs / p.unit;
-    return (int64_t)c * units / gridDim.x * p.unit;
+    const uint32_t units = p.units;
+    return (int64_t)((uint32_t)c * units / gridDim.x) * p.unit;
 }
 // CTA whose range holds pair u.
 __device__ __forceinline__ int owner_of(const DqmmParams& p, int64_t u) {
-    const int64_t units = p.total_pairs / p.unit;
-    return (int)(((u / p.unit + 1) * (int64_t)gridDim.x - 1) / units);
+    const uint32_t units = p.units;
+    return (int)((((uint32_t)u / (uint32_t)p.unit + 1u) * gridDim.x - 1u) / units);
 }
 __device__ __forceinline__ Seg segment_at(const DqmmParams& p, int64_t u, int64_t u_end) {
     const int P = p.n_kb / 2;
     Seg g;
-    g.tile = (int)(u / P);
+    g.tile = (int)((uint32_t)u / (uint32_t)P);
     const int pb = (int)(u - (int64_t)g.tile * P);
     const int64_t left = u_end - u;
     const int pe = (int64_t)(P - pb) < left ? P : (int)(pb + left);
@@ -1050,6 +1054,14 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     const int n_tok_tiles = (int)((a.M + BT - 1) / BT);
     prm.n_items = prm.n_row_tiles * n_tok_tiles;
     prm.total_pairs = L.total_pairs;
+    {
+        const int64_t units = L.total_pairs / L.unit;
+        if (units * (int64_t)(L.grid + 1) >= (int64_t)1 << 32 || L.total_pairs >= (int64_t)1 << 32) {
+            *why = "work split exceeds 32-bit indexing (shape too large)";
+            return PN_ERR_UNSUPPORTED;
+        }
+        prm.units = (uint32_t)units;
+    }
     prm.unit = L.unit;
     prm.accbuf = ws + L.accbuf;
     prm.acc_cols = L.acc_cols;
