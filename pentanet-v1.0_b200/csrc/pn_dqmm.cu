@@ -830,23 +830,25 @@ __global__ void __launch_bounds__(256) permute_x_kernel(const __nv_bfloat16* __r
     // the GEMM's split-tile counters and sums start at zero
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_zero16; i += (int64_t)gridDim.x * blockDim.x)
         zero[i] = make_uint4(0, 0, 0, 0);
-    const int64_t kpad = (int64_t)n_kb * kKB;
-    const int64_t total = (int64_t)M * kpad;
-    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-         idx += (int64_t)gridDim.x * blockDim.x) {
-        const int m = (int)(idx / kpad);
-        const int64_t kk = idx - (int64_t)m * kpad;
-        const int64_t g = kk / kPerWord;
+    // 32-bit index arithmetic (the host checks M * n_kb * 160 < 2^31): this
+    // grid runs beside the GEMM's unpack warps and should take few of their
+    // issue slots.
+    const uint32_t kpad = (uint32_t)n_kb * kKB;
+    const uint32_t total = (uint32_t)M * kpad;
+    for (uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+        const uint32_t m = idx / kpad;
+        const uint32_t kk = idx - m * kpad;
+        const uint32_t g = kk / kPerWord;
         const int q = (int)(kk - g * kPerWord);
-        const int64_t ksrc = g * kPerWord + perm_src(q);
-        float v = ksrc < K ? __bfloat162float(x[(int64_t)m * K + ksrc]) : 0.0f;
+        const uint32_t ksrc = g * kPerWord + perm_src(q);
+        float v = ksrc < (uint64_t)K ? __bfloat162float(x[(int64_t)m * K + ksrc]) : 0.0f;
         v = __fmul_rn(v, __int_as_float((127 - perm_exp(q)) << 23));  // * 2^-perm_exp(q), exact
-        const int64_t kb = kk / kKB;
-        const int e = (int)(kk - kb * kKB);
-        const int j = e >> 4;
-        const int ee = e & 15;
-        const int h = (ee >> 3) ^ ((m >> 2) & 1);
-        const size_t off = (size_t)kb * (BT * 32 * 10) + (size_t)j * BT * 32 + m * 32 + h * 16 + (ee & 7) * 2;
+        const uint32_t kb = kk / kKB;
+        const uint32_t e = kk - kb * kKB;
+        const uint32_t j = e >> 4;
+        const uint32_t ee = e & 15;
+        const uint32_t h = (ee >> 3) ^ ((m >> 2) & 1);
+        const size_t off = (size_t)kb * (BT * 32 * 10) + j * BT * 32 + m * 32 + h * 16 + (ee & 7) * 2;
         *reinterpret_cast<__nv_bfloat16*>(out + off) = __float2bfloat16_rn(v);
     }
 }
@@ -1072,6 +1074,10 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     const int64_t n_zero16 = L.unit == 1 ? (int64_t)(L.zero_bytes / 16) : 0;
     if (C::kPerm) {
         const int64_t total = a.M * (int64_t)prm.n_kb * kKB;
+        if (total >= (int64_t)1 << 31) {
+            *why = "activation re-layout exceeds 32-bit indexing (K too large)";
+            return PN_ERR_UNSUPPORTED;
+        }
         int64_t want = (total + 255) / 256;
         if (n_zero16 / 1024 > want) want = n_zero16 / 1024;  // ~4 zeroing stores per thread
         const int blocks = (int)(want < 1024 ? (want > 0 ? want : 1) : 1024);
