@@ -323,6 +323,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
+    // The next product on the stream (its decode pre-pass, launched as a
+    // programmatic dependent) may be scheduled now: it waits for this grid's
+    // completion before it touches memory, and the GEMM after it starts its
+    // prologue and weight streaming on the SMs this grid frees.
+    asm volatile("griddepcontrol.launch_dependents;");
+
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kSW; ++s) {
             mbar_init(&full_w[s], 1);
@@ -819,14 +825,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 // x 32 bytes, 32-byte swizzled, each 10-group of k permuted by perm_src and
 // scaled by 2^-perm_exp (exact).  Positions past K are zero; rows >= M are not
 // written (their accumulator columns are never read back).
+constexpr int kPermThreads = 256;
 template <int BT>
-__global__ void __launch_bounds__(256) permute_x_kernel(const __nv_bfloat16* __restrict__ x, int M, int64_t K,
+__global__ void __launch_bounds__(kPermThreads) permute_x_kernel(const __nv_bfloat16* __restrict__ x, int M, int64_t K,
                                                         int n_kb, uint8_t* __restrict__ out, uint4* __restrict__ zero,
                                                         int64_t n_zero16) {
     // The GEMM launched after this kernel (programmatic dependent launch) may
     // start its prologue and weight streaming now; it waits for this grid's
     // results before it reads them.
     asm volatile("griddepcontrol.launch_dependents;");
+    // This grid may itself be a programmatic dependent of the previous product
+    // on the stream (whose output can be this x, and whose workspace this one
+    // can reuse): nothing is read or written before that grid has completed.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     // the GEMM's split-tile counters and sums start at zero
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_zero16; i += (int64_t)gridDim.x * blockDim.x)
         zero[i] = make_uint4(0, 0, 0, 0);
@@ -1078,11 +1089,37 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
             *why = "activation re-layout exceeds 32-bit indexing (K too large)";
             return PN_ERR_UNSUPPORTED;
         }
-        int64_t want = (total + 255) / 256;
-        if (n_zero16 / 1024 > want) want = n_zero16 / 1024;  // ~4 zeroing stores per thread
+        int64_t want = (total + kPermThreads - 1) / kPermThreads;
+        if (n_zero16 / (4 * kPermThreads) > want) want = n_zero16 / (4 * kPermThreads);  // ~4 zeroing stores per thread
         const int blocks = (int)(want < 1024 ? (want > 0 ? want : 1) : 1024);
-        permute_x_kernel<BT><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(a.x), (int)a.M, a.K, prm.n_kb,
-                                                    ws + L.xperm, reinterpret_cast<uint4*>(ws + L.counters), n_zero16);
+        const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(a.x);
+        uint4* zero = reinterpret_cast<uint4*>(ws + L.counters);
+        cudaError_t e;
+        if (!repitch) {
+            // a programmatic dependent of the previous kernel on the stream
+            // (the kernel waits for it before touching memory); with a
+            // re-pitched weight copy the GEMM's weight loads depend on the
+            // copy kernel, so then the launch is fully serialised
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(blocks);
+            cfg.blockDim = dim3(kPermThreads);
+            cfg.stream = s;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            e = cudaLaunchKernelEx(&cfg, permute_x_kernel<BT>, xb, (int)a.M, a.K, prm.n_kb, ws + L.xperm, zero,
+                                   n_zero16);
+        } else {
+            permute_x_kernel<BT><<<blocks, kPermThreads, 0, s>>>(xb, (int)a.M, a.K, prm.n_kb, ws + L.xperm, zero, n_zero16);
+            e = cudaGetLastError();
+        }
+        if (e != cudaSuccess) {
+            *err = e;
+            *why = "activation re-layout launch";
+            return PN_ERR_CUDA;
+        }
     } else if (n_zero16 > 0) {
         cudaError_t e = cudaMemsetAsync(ws + L.counters, 0, L.zero_bytes, s);
         if (e != cudaSuccess) {
