@@ -68,6 +68,13 @@ int pn_absmean_scale(const void *w, int w_dtype, int64_t n_elems, float *d_scale
 int pn_quantize_pack(const void *w, int w_dtype, int64_t N, int64_t K, const float *d_scale,
                      int32_t *packed, void *stream);
 
+/* The ternary (BitNet) rule of the reference's QuantLinear(mode='bitnet')
+ * (train_pentagpt.py:33-36): q = clamp(round_half_even(W / gamma), -1, 1)
+ * with the same absmean gamma, stored in the same 3-bit codes (q + 2), so
+ * every product entry point runs ternary layers unchanged. */
+int pn_quantize_pack_ternary(const void *w, int w_dtype, int64_t N, int64_t K, const float *d_scale,
+                             int32_t *packed, void *stream);
+
 /* ---- unpack: replaces unpack_weights (penta_kernel.py:81-90) and the C
  *      penta_unpack_3bit (penta_avx2.c:41-59) ------------------------------- */
 

@@ -50,6 +50,8 @@ def lib() -> ctypes.CDLL:
         L.pno_absmean_scale.argtypes = [P, I64]
         L.pno_quantize_pack.restype = None
         L.pno_quantize_pack.argtypes = [P, I64, I64, ctypes.c_float, P]
+        L.pno_quantize_pack_ternary.restype = None
+        L.pno_quantize_pack_ternary.argtypes = [P, I64, I64, ctypes.c_float, P]
         L.pno_unpack.restype = None
         L.pno_unpack.argtypes = [P, I64, I64, I64, P]
         L.pno_matmul_f32.restype = None
@@ -82,14 +84,17 @@ def absmean_scale(w: np.ndarray) -> float:
     return float(lib().pno_absmean_scale(_p(w), w.size))
 
 
-def quantize_pack(w: np.ndarray, gamma: float | None = None):
-    """quantize_and_pack (penta_kernel.py:42-78) -> (packed int32 (N,KP), K, gamma)."""
+def quantize_pack(w: np.ndarray, gamma: float | None = None, mode: str = "pentanet"):
+    """quantize_and_pack (penta_kernel.py:42-78) -> (packed int32 (N,KP), K, gamma).
+    mode 'bitnet': the ternary rule of QuantLinear (train_pentagpt.py:33-36),
+    clamp to [-1, 1], in the same 3-bit codes."""
     w = np.ascontiguousarray(w, dtype=np.float32)
     N, K = w.shape
     if gamma is None:
         gamma = absmean_scale(w)
     packed = np.empty((N, k_packs(K)), dtype=np.int32)
-    lib().pno_quantize_pack(_p(w), N, K, ctypes.c_float(gamma), _p(packed))
+    fn = lib().pno_quantize_pack_ternary if mode == "bitnet" else lib().pno_quantize_pack
+    fn(_p(w), N, K, ctypes.c_float(gamma), _p(packed))
     return packed, K, float(np.float32(gamma))
 
 

@@ -45,19 +45,19 @@ float pno_absmean_scale(const float *w, int64_t n) {
  * (penta_kernel.py:60).  NaN has no defined result in the reference (its
  * int32 cast is platform dependent); it is mapped to 0 here and in the
  * CUDA kernel. */
-static inline int pno_quant1(float w, float gamma) {
+static inline int pno_quant1(float w, float gamma, float qmax) {
     float t = w / gamma;                 /* IEEE float division */
     if (t != t) return 0;                /* NaN */
     float r = nearbyintf(t);             /* round half to even */
-    if (r < -2.0f) r = -2.0f;
-    if (r > 2.0f) r = 2.0f;
+    if (r < -qmax) r = -qmax;
+    if (r > qmax) r = qmax;
     return (int)r;
 }
 
 /* quantize_and_pack body for a given gamma (penta_kernel.py:60-78):
  * code = q + 2 (:70), packed |= code << 3i (:74-76), pad with code 2 (:62-65). */
-void pno_quantize_pack(const float *w, int64_t N, int64_t K, float gamma,
-                       int32_t *packed) {
+static void pno_quantize_pack_q(const float *w, int64_t N, int64_t K, float gamma,
+                                int32_t *packed, float qmax) {
     const int64_t KP = pno_k_packs(K);
     for (int64_t n = 0; n < N; ++n) {
         const float *row = w + n * K;
@@ -65,12 +65,23 @@ void pno_quantize_pack(const float *w, int64_t N, int64_t K, float gamma,
             uint32_t word = 0;
             for (int i = 0; i < PNO_PER_WORD; ++i) {
                 int64_t k = g * PNO_PER_WORD + i;
-                uint32_t code = (k < K) ? (uint32_t)(pno_quant1(row[k], gamma) + 2) : 2u;
+                uint32_t code = (k < K) ? (uint32_t)(pno_quant1(row[k], gamma, qmax) + 2) : 2u;
                 word |= code << (3 * i);
             }
             packed[n * KP + g] = (int32_t)word;
         }
     }
+}
+
+void pno_quantize_pack(const float *w, int64_t N, int64_t K, float gamma, int32_t *packed) {
+    pno_quantize_pack_q(w, N, K, gamma, packed, 2.0f);
+}
+
+/* The ternary (BitNet) mode of the reference's QuantLinear
+ * (train_pentagpt.py:33-36): clamp(round(w / gamma), -1, 1), same absmean
+ * gamma, stored in the same 3-bit codes (q + 2 in {1, 2, 3}). */
+void pno_quantize_pack_ternary(const float *w, int64_t N, int64_t K, float gamma, int32_t *packed) {
+    pno_quantize_pack_q(w, N, K, gamma, packed, 1.0f);
 }
 
 /* unpack_weights / penta_unpack_3bit (penta_kernel.py:81-90,

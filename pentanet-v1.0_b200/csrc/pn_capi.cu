@@ -116,8 +116,8 @@ int pn_absmean_scale(const void* w, int w_dtype, int64_t n_elems, float* d_scale
     return e == cudaSuccess ? ok() : cuda_fail(e, "pn_absmean_scale");
 }
 
-int pn_quantize_pack(const void* w, int w_dtype, int64_t N, int64_t K, const float* d_scale, int32_t* packed,
-                     void* stream) {
+static int quantize_pack_impl(const void* w, int w_dtype, int64_t N, int64_t K, const float* d_scale,
+                              int32_t* packed, int qmax, void* stream) {
     if (!d_scale || ((!w || !packed) && N > 0)) return fail(PN_ERR_ARG, "pn_quantize_pack: null pointer");
     if (w_dtype != PN_F32 && w_dtype != PN_BF16) return fail(PN_ERR_DTYPE, "pn_quantize_pack: dtype %d", w_dtype);
     if (N < 0 || K < 1) return fail(PN_ERR_SHAPE, "pn_quantize_pack: N=%lld K=%lld", (long long)N, (long long)K);
@@ -125,8 +125,18 @@ int pn_quantize_pack(const void* w, int w_dtype, int64_t N, int64_t K, const flo
         return fail(PN_ERR_ALIGN, "pn_quantize_pack: misaligned pointer");
     if (int st = check_device()) return st;
     if (N == 0) return ok();
-    cudaError_t e = pn::launch_quantize_pack(w, w_dtype, N, K, d_scale, packed, (cudaStream_t)stream);
+    cudaError_t e = pn::launch_quantize_pack(w, w_dtype, N, K, d_scale, packed, qmax, (cudaStream_t)stream);
     return e == cudaSuccess ? ok() : cuda_fail(e, "pn_quantize_pack");
+}
+
+int pn_quantize_pack(const void* w, int w_dtype, int64_t N, int64_t K, const float* d_scale, int32_t* packed,
+                     void* stream) {
+    return quantize_pack_impl(w, w_dtype, N, K, d_scale, packed, 2, stream);
+}
+
+int pn_quantize_pack_ternary(const void* w, int w_dtype, int64_t N, int64_t K, const float* d_scale,
+                             int32_t* packed, void* stream) {
+    return quantize_pack_impl(w, w_dtype, N, K, d_scale, packed, 1, stream);
 }
 
 int pn_unpack(const int32_t* packed, int64_t N, int64_t K_packs, int64_t K_orig, int8_t* out, void* stream) {

@@ -9,7 +9,7 @@ namespace pn {
 size_t absmean_workspace_bytes();
 cudaError_t launch_absmean(const void* w, int dtype, int64_t n, float* d_scale, void* ws, cudaStream_t s);
 cudaError_t launch_quantize_pack(const void* w, int dtype, int64_t N, int64_t K, const float* d_scale,
-                                 int32_t* packed, cudaStream_t s);
+                                 int32_t* packed, int qmax, cudaStream_t s);
 cudaError_t launch_unpack(const int32_t* packed, int64_t N, int64_t KP, int64_t K, int8_t* out, cudaStream_t s);
 
 int64_t act_i8_pitch(int64_t K);

@@ -64,10 +64,12 @@ __global__ void __launch_bounds__(kAbsBlocks) absmean_final_kernel(const double*
 
 // One thread per packed word.  NaN quantises to 0 (the reference leaves it
 // platform-defined); +-inf saturate to +-2 like clamp does.
+// qmax 2: pentanary (penta_kernel.py:60); qmax 1: the ternary (BitNet) rule
+// of the reference's QuantLinear (train_pentagpt.py:33-36) in the same codes.
 template <typename T>
 __global__ void __launch_bounds__(256) quantize_pack_kernel(const T* __restrict__ w, int64_t N, int64_t K,
                                                             int64_t KP, const float* __restrict__ d_scale,
-                                                            int32_t* __restrict__ packed) {
+                                                            int32_t* __restrict__ packed, float qmax) {
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= N * KP) return;
     const float gamma = __ldg(d_scale);
@@ -82,7 +84,7 @@ __global__ void __launch_bounds__(256) quantize_pack_kernel(const T* __restrict_
         if (k < K) {
             const float t = __fdiv_rn(load_as_float(row, k), gamma);
             float r = rintf(t);  // round half to even
-            r = fminf(fmaxf(r, -2.0f), 2.0f);
+            r = fminf(fmaxf(r, -qmax), qmax);
             code = (t != t) ? 2u : (uint32_t)((int)r + 2);
         }
         word |= code << (3 * i);
@@ -120,15 +122,16 @@ cudaError_t launch_absmean(const void* w, int dtype, int64_t n, float* d_scale, 
 }
 
 cudaError_t launch_quantize_pack(const void* w, int dtype, int64_t N, int64_t K, const float* d_scale,
-                                 int32_t* packed, cudaStream_t s) {
+                                 int32_t* packed, int qmax, cudaStream_t s) {
     const int64_t KP = (K + kPerWord - 1) / kPerWord;
     const int64_t total = N * KP;
     const unsigned blocks = (unsigned)((total + 255) / 256);
     if (dtype == PN_F32)
-        quantize_pack_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(w), N, K, KP, d_scale, packed);
+        quantize_pack_kernel<float>
+            <<<blocks, 256, 0, s>>>(static_cast<const float*>(w), N, K, KP, d_scale, packed, (float)qmax);
     else
         quantize_pack_kernel<__nv_bfloat16>
-            <<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(w), N, K, KP, d_scale, packed);
+            <<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(w), N, K, KP, d_scale, packed, (float)qmax);
     return cudaGetLastError();
 }
 

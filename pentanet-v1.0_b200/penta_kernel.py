@@ -66,7 +66,7 @@ def absmean_scale(weight: torch.Tensor) -> torch.Tensor:
     return out
 
 
-def quantize_and_pack(weight: torch.Tensor, scale: float | torch.Tensor | None = None
+def quantize_and_pack(weight: torch.Tensor, scale: float | torch.Tensor | None = None, mode: str = 'pentanet'
                       ) -> tuple[torch.Tensor, int, float]:
     """Quantize FP32/BF16 master weights to pentanary {-2..+2} and 3-bit pack.
 
@@ -74,6 +74,10 @@ def quantize_and_pack(weight: torch.Tensor, scale: float | torch.Tensor | None =
         weight : (N, K) FP32/BF16 CUDA tensor
         scale  : optional absmean scale to use instead of computing it (a float
                  or a 0-dim CUDA tensor); the reference always computes it.
+        mode   : 'pentanet' (the reference's rule) or 'bitnet': the ternary
+                 {-1, 0, +1} rule of QuantLinear(mode='bitnet')
+                 (train_pentagpt.py:33-36), stored in the same 3-bit codes so
+                 that every product runs it unchanged (not in the reference).
 
     Returns:
         packed : (N, ceil(K/10)) int32, byte-identical to the reference
@@ -81,6 +85,7 @@ def quantize_and_pack(weight: torch.Tensor, scale: float | torch.Tensor | None =
         scale  : python float (penta_kernel.py:57)
     """
     assert weight.dim() == 2
+    assert mode in ('pentanet', 'bitnet'), f"unknown mode {mode!r}"
     _require_cuda(weight, "quantize_and_pack")
     N, K = weight.shape
     w = weight.detach().contiguous()
@@ -94,8 +99,10 @@ def quantize_and_pack(weight: torch.Tensor, scale: float | torch.Tensor | None =
         d_scale = torch.tensor(float(scale), dtype=torch.float32, device=w.device)
     packed = torch.empty(N, _k_packs(K), dtype=torch.int32, device=w.device)
     dt = _nat.PN_F32 if w.dtype == torch.float32 else _nat.PN_BF16
-    _nat.check(_nat.load().pn_quantize_pack(w.data_ptr(), dt, N, K, d_scale.data_ptr(), packed.data_ptr(),
-                                            _nat.stream_of(w)), "quantize_and_pack")
+    L = _nat.load()
+    fn = L.pn_quantize_pack_ternary if mode == 'bitnet' else L.pn_quantize_pack
+    _nat.check(fn(w.data_ptr(), dt, N, K, d_scale.data_ptr(), packed.data_ptr(), _nat.stream_of(w)),
+               "quantize_and_pack")
     return packed, K, float(d_scale)
 
 

@@ -23,7 +23,7 @@ PN_F32, PN_BF16, PN_I8, PN_I32 = 0, 1, 2, 3
 # Functions the header declares; tests check the library exports each one.
 EXPORTS = (
     "pn_abi_version", "pn_status_string", "pn_last_error", "pn_device_status", "pn_device_sm_count",
-    "pn_absmean_workspace_size", "pn_absmean_scale", "pn_quantize_pack", "pn_unpack",
+    "pn_absmean_workspace_size", "pn_absmean_scale", "pn_quantize_pack", "pn_quantize_pack_ternary", "pn_unpack",
     "pn_linear_workspace_size", "pn_linear_workspace_min_size", "pn_linear_bf16", "pn_linear_bf16_ld", "pn_packed_ld",
     "pn_linear_bf16_nows", "pn_act_i8_pitch", "pn_quant_act_i8", "pn_linear_i8", "pn_linear_i8_ld",
     "pn_ipc_handle", "pn_ipc_open", "pn_ipc_close",
@@ -61,6 +61,7 @@ def load() -> ctypes.CDLL:
         "pn_absmean_workspace_size": (SZ, []),
         "pn_absmean_scale": (I, [P, I, I64, P, P, SZ, P]),
         "pn_quantize_pack": (I, [P, I, I64, I64, P, P, P]),
+        "pn_quantize_pack_ternary": (I, [P, I, I64, I64, P, P, P]),
         "pn_unpack": (I, [P, I64, I64, I64, P, P]),
         "pn_linear_workspace_size": (SZ, [I, I64, I64, I64]),
         "pn_linear_workspace_min_size": (SZ, [I, I64, I64, I64]),

@@ -83,8 +83,10 @@ class PentaLinearFast(nn.Module):
     @classmethod
     def from_pentalinear(cls, layer: nn.Module, act_quant: str | None = None) -> 'PentaLinearFast':
         """Quantize + 3-bit pack the master weights of a trained PentaLinear (or
-        QuantLinear in pentanet mode)."""
-        packed, K_orig, scale = quantize_and_pack(layer.weight.detach())
+        QuantLinear in pentanet mode; in bitnet mode with its ternary rule,
+        train_pentagpt.py:33-36, in the same codes)."""
+        mode = 'bitnet' if getattr(layer, 'mode', 'pentanet') == 'bitnet' else 'pentanet'
+        packed, K_orig, scale = quantize_and_pack(layer.weight.detach(), mode=mode)
         bias = layer.bias.detach().clone() if getattr(layer, 'bias', None) is not None else None
         return cls(packed, scale, K_orig, bias, act_quant=act_quant)
 
@@ -124,15 +126,15 @@ class PentaLinearFast(nn.Module):
 def _is_pentanary_layer(module: nn.Module) -> bool:
     if isinstance(module, PentaLinear):
         return True
-    # train_pentagpt.QuantLinear (train_pentagpt.py:16-40) in pentanet mode
-    return (type(module).__name__ == 'QuantLinear' and getattr(module, 'mode', None) == 'pentanet'
+    # train_pentagpt.QuantLinear (train_pentagpt.py:16-40), pentanet or bitnet mode
+    return (type(module).__name__ == 'QuantLinear' and getattr(module, 'mode', None) in ('pentanet', 'bitnet')
             and isinstance(getattr(module, 'weight', None), torch.Tensor) and module.weight.dim() == 2)
 
 
 def convert_to_fast_inference(model: nn.Module, act_quant: str | None = None) -> nn.Module:
-    """Recursively convert every PentaLinear (and QuantLinear(mode='pentanet'))
-    layer to PentaLinearFast (pentanet_layer.py:137-153).  Tied weights are
-    packed once per distinct parameter."""
+    """Recursively convert every PentaLinear (and QuantLinear, mode 'pentanet'
+    or the ternary 'bitnet') layer to PentaLinearFast (pentanet_layer.py:137-153).
+    Tied weights are packed once per distinct parameter."""
     cache: dict[int, PentaLinearFast] = {}
 
     def rec(m: nn.Module) -> None:

@@ -46,7 +46,8 @@ class QuantLinear(nn.Module):
 
     def forward(self, x):
         scale = self.weight.abs().mean().clamp(min=1e-8)
-        w_q = torch.clamp(torch.round(self.weight / scale), -2, 2)
+        qmax = 2 if self.mode == "pentanet" else 1   # train_pentagpt.py:32-36
+        w_q = torch.clamp(torch.round(self.weight / scale), -qmax, qmax)
         return nn.functional.linear(x, (w_q * scale - self.weight).detach() + self.weight)
 
 
@@ -65,7 +66,7 @@ def test_convert_model_with_quantlinear_and_tied(cuda_device):
         y_ref = m(x)
     convert_to_fast_inference(m)
     assert isinstance(m[0], PentaLinearFast) and isinstance(m[2], PentaLinearFast)
-    assert isinstance(m[3], QuantLinear)         # bitnet mode is not pentanary
+    assert isinstance(m[3], PentaLinearFast)     # ternary (bitnet) layers pack into the same codes
     assert isinstance(m[4], PentaLinearFast)
     with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
         y = m(x)
@@ -100,3 +101,20 @@ def test_int8_activation_mode(cuda_device):
         y_ref = layer(x)
     # per-token int8 activations: the quantisation error, not kernel error, dominates
     assert (y.float() - y_ref).abs().max() < 0.5
+
+
+def test_ternary_pack_and_product(cuda_device):
+    """mode='bitnet': the ternary rule of QuantLinear (train_pentagpt.py:33-36)
+    in the same 3-bit codes; packed bytes equal the oracle's, every code is in
+    {1, 2, 3}, and the bf16 product matches the oracle."""
+    w = torch.randn(300, 1001, generator=torch.Generator().manual_seed(7)) * 0.02
+    packed, K, gamma = pk.quantize_and_pack(w.to(cuda_device), mode="bitnet")
+    want, _, g_want = orc.quantize_pack(w.numpy(), mode="bitnet")
+    assert np.array_equal(packed.cpu().numpy(), want)
+    w8 = orc.unpack(want, K)
+    assert w8.min() == -1 and w8.max() == 1
+    penta, _, _ = pk.quantize_and_pack(w.to(cuda_device))
+    assert not np.array_equal(packed.cpu().numpy(), penta.cpu().numpy())
+    x = torch.randn(5, K, generator=torch.Generator().manual_seed(8)).to(torch.bfloat16)
+    y = pk.penta_linear(x.to(cuda_device), packed, gamma, K, out_dtype=torch.float32)
+    assert_close(y.cpu().numpy(), orc.matmul_f64(x.float().numpy(), w8, gamma), what="ternary")

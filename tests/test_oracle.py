@@ -148,3 +148,16 @@ def test_memory_stats_matches_reference():
     for key, stats in META["memory_stats"].items():
         N, K = map(int, key.split("x"))
         assert pk.memory_stats(N, K) == stats
+
+
+def test_ternary_rule():
+    """The oracle's ternary (bitnet) quantiser is clamp(round_half_even(w / gamma),
+    -1, 1) with float32 division (train_pentagpt.py:33-36), ties included."""
+    w = gen_weight(64, 257, seed=3).numpy()
+    w[0, :4] = [0.5, -0.5, 1.5, -2.5]
+    gamma = 1.0
+    packed, K, _ = orc.quantize_pack(w, gamma, mode="bitnet")
+    q = orc.unpack(packed, K)
+    want = np.clip(np.rint(w.astype(np.float32) / np.float32(gamma)), -1, 1).astype(np.int8)
+    assert np.array_equal(q, want)
+    assert list(q[0, :4]) == [0, 0, 1, -1]
