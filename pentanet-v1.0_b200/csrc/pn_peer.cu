@@ -23,6 +23,10 @@ struct PeerFlags {
 };
 
 __global__ void __launch_bounds__(32) peer_barrier_kernel(PeerFlags f, int world, int rank, int* gen) {
+    // The next product's pre-pass (a programmatic dependent) may be scheduled
+    // during the exchange: it waits for this grid's completion before it
+    // touches memory, and the GEMM after it starts streaming weights.
+    asm volatile("griddepcontrol.launch_dependents;");
     const int lane = threadIdx.x;
     int g = 0;
     if (lane == 0) {

@@ -76,3 +76,26 @@ def test_peer_outputs_world1(cuda_device, tmp_path):
 def test_peer_outputs_world2(cuda_device, tmp_path):
     mp.start_processes(_run, args=(2, _free_port(), str(tmp_path), CASES), nprocs=2, start_method="spawn")
     _check(str(tmp_path), 2)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 300, 1000), (16, 256, 4096), (64, 384, 3072), (200, 256, 1600)])
+def test_two_outputs_one_gpu(cuda_device, M, N, K):
+    """The multi-output epilogue on one GPU: the shard's columns stored into two
+    local buffers (row stride ld > N, first column col0) equal the plain product,
+    and nothing outside the shard's columns is written."""
+    import ctypes
+    import penta_kernel as pk
+    import penta_native as nat
+    import penta_dist as pd
+    packed, _, gamma = pk.quantize_and_pack(gen_weight(N, K, seed=M + K).to(cuda_device))
+    x = gen_act(M, K, seed=N).to(torch.bfloat16).to(cuda_device)
+    want = pk.penta_linear(x, packed, gamma, K)
+    ld, col0 = N + 24, 16
+    bufs = [torch.full((M, ld), 7.0, dtype=torch.bfloat16, device=cuda_device) for _ in range(2)]
+    for _ in range(2):  # two calls in a row
+        pd.linear_peers(x, packed, gamma, K, col0, [b.data_ptr() for b in bufs], ld)
+        torch.cuda.synchronize()
+        for b in bufs:
+            assert torch.equal(b[:, col0:col0 + N], want)
+            assert bool((b[:, :col0] == 7.0).all()) and bool((b[:, col0 + N:] == 7.0).all())
+    assert nat.device_status() == 0
