@@ -680,10 +680,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                     yp[(int64_t)j * p.N] = __float2bfloat16_rn(yv);
                 }
             };
-            const bool fast_out = p.n_out == 1 && !p.y_f32 && p.bias == nullptr && p.acc_out == nullptr;
+            // The same for output-sharded products: the 16 values are computed
+            // once, then each output buffer gets one straight run of stores.
+            auto finish_fast_multi = [&](int c0, const uint32_t (&acc)[16]) {
+                if (n >= p.N) return;
+                __nv_bfloat16 v[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    float yv;
+                    if constexpr (KIND == Kind::F16) {
+                        yv = __fmul_rn(__uint_as_float(acc[j]), p.scale);
+                    } else {
+                        const int m = m0 + c0 + j;
+                        const int acc_i = (int)acc[j] - 2 * __ldg(p.rowsum + m);
+                        yv = __fmul_rn((float)acc_i, __fmul_rn(p.scale, __ldg(p.s_x + m)));
+                    }
+                    v[j] = __float2bfloat16_rn(yv);
+                }
+                const int64_t off = (int64_t)(m0 + c0) * p.ld_y + p.y_col0 + n;
+                for (int r = 0; r < p.n_out; ++r) {
+                    __nv_bfloat16* yp = static_cast<__nv_bfloat16*>(p.y_out[r]) + off;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) yp[(int64_t)j * p.ld_y] = v[j];
+                }
+            };
+            const bool plain_out = !p.y_f32 && p.bias == nullptr && p.acc_out == nullptr;
+            const bool fast_out = p.n_out == 1 && plain_out;
             auto finish = [&](int c0, const uint32_t (&acc)[16]) {
                 if (fast_out && m0 + c0 + 16 <= p.M)
                     finish_fast(c0, acc);
+                else if (p.n_out > 1 && plain_out && m0 + c0 + 16 <= p.M)
+                    finish_fast_multi(c0, acc);
                 else if (p.n_out > 1)
                     finish_t(std::true_type{}, c0, acc);
                 else
