@@ -14,6 +14,14 @@ float64 and the total element count), so every shard quantises exactly as the
 unsharded layer would.  Each rank runs the local tensor-core GEMV/GEMM on its
 rows and the shards meet in one NCCL all-gather; the reference has no
 multi-GPU path (its multi-"GPU" runs are independent jobs).
+
+A column-parallel layer and its row-parallel partner (an MLP's up and down
+projections) need no gather at all: `ShardedPentaLinear(gather=False)` keeps
+each rank's block of the up projection's outputs on that rank, and
+`RowShardedPentaLinear` multiplies that block by its K slice of the down
+projection's packed weights, so one all-reduce of fp32 partial products per
+pair replaces an all-gather per layer.  Both shard with boundaries on
+multiples of 40 columns, so every K slice starts on a packed word.
 """
 from __future__ import annotations
 
@@ -30,8 +38,15 @@ except ImportError:
     import penta_native as nat
 
 
-def shard_range(N: int, rank: int, world: int) -> tuple[int, int]:
-    """Rows [lo, hi) owned by `rank`; remainders go to the lowest ranks."""
+def shard_range(N: int, rank: int, world: int, unit: int = 1) -> tuple[int, int]:
+    """Rows [lo, hi) owned by `rank`; remainders go to the lowest ranks.  With
+    unit > 1 the boundaries fall on multiples of `unit` (the last shard ends at
+    N): a column-parallel layer sharded with unit 40 hands a row-parallel
+    partner K slices that start on packed words (10 k each) at 16-byte
+    aligned activation offsets."""
+    if unit > 1:
+        lo_u, hi_u = shard_range((N + unit - 1) // unit, rank, world)
+        return min(lo_u * unit, N), min(hi_u * unit, N)
     base, rem = divmod(N, world)
     lo = rank * base + min(rank, rem)
     return lo, lo + base + (1 if rank < rem else 0)
@@ -53,28 +68,46 @@ def global_absmean(local_weight: torch.Tensor, group=None) -> torch.Tensor:
 
 
 def gather_columns(y_local: torch.Tensor, N: int, world: int, group=None,
-                   out: torch.Tensor | None = None) -> torch.Tensor:
-    """All-gather per-rank (M, N/P) output blocks into the full (M, N) result.
-    Requires N divisible by the world size (all 7B/70B shapes at P <= 8)."""
+                   out: torch.Tensor | None = None, unit: int = 1) -> torch.Tensor:
+    """All-gather the per-rank (M, hi - lo) output blocks, rank r owning the
+    columns shard_range(N, r, world, unit), into the full (M, N) result.
+    Equal shards (all 7B/70B shapes at P <= 8) gather in place; unequal ones
+    are padded to the largest shard for the collective."""
     M, n_loc = y_local.shape
-    assert n_loc * world == N, "gather_columns needs equal shards"
-    # rank-major concatenation along dim 0 (the layout every backend accepts)
-    buf = torch.empty(world * M, n_loc, dtype=y_local.dtype, device=y_local.device)
-    dist.all_gather_into_tensor(buf, y_local.contiguous(), group=group)
+    ranges = [shard_range(N, r, world, unit) for r in range(world)]
+    lo, hi = ranges[dist.get_rank(group)]
+    assert n_loc == hi - lo, f"this rank owns {hi - lo} columns, got {n_loc}"
+    n_max = max(b - a for a, b in ranges)
     if out is None:
         out = torch.empty(M, N, dtype=y_local.dtype, device=y_local.device)
-    out.view(M, world, n_loc).copy_(buf.view(world, M, n_loc).permute(1, 0, 2))
+    src = y_local.contiguous()
+    if n_loc != n_max:
+        src = torch.zeros(M, n_max, dtype=y_local.dtype, device=y_local.device)
+        src[:, :n_loc] = y_local
+    # rank-major concatenation along dim 0 (the layout every backend accepts)
+    buf = torch.empty(world * M, n_max, dtype=y_local.dtype, device=y_local.device)
+    dist.all_gather_into_tensor(buf, src, group=group)
+    if n_max * world == N:
+        out.view(M, world, n_max).copy_(buf.view(world, M, n_max).permute(1, 0, 2))
+    else:
+        blocks = buf.view(world, M, n_max)
+        for r, (a, b) in enumerate(ranges):
+            out[:, a:b].copy_(blocks[r, :, :b - a])
     return out
 
 
 class ShardedPentaLinear(torch.nn.Module):
     """PentaLinearFast split by output rows over the ranks of `group`; forward
-    returns the full (..., N) output on every rank."""
+    returns the full (..., N) output on every rank, or with gather=False this
+    rank's (..., hi - lo) block of columns [lo, hi) (the input of a
+    RowShardedPentaLinear partner, which then needs no gather)."""
 
     def __init__(self, packed_local: torch.Tensor, scale: float, K_orig: int, N: int,
                  bias_local: torch.Tensor | None = None, group=None, act_quant: str | None = None,
-                 peers: "PeerGroup | None" = None, max_tokens: int = 64):
+                 peers: "PeerGroup | None" = None, max_tokens: int = 64, gather: bool = True, unit: int = 1):
         super().__init__()
+        self.gather = gather
+        self.unit = int(unit)
         self.register_buffer("packed_w", packed_local)
         self.scale = float(scale)
         self.K_orig = int(K_orig)
@@ -88,17 +121,19 @@ class ShardedPentaLinear(torch.nn.Module):
         # buffer and is overwritten by the next forward of this layer.
         self.peers = peers
         if peers is not None:
-            self.col0 = shard_range(self.N, peers.rank, peers.world)[0]
+            assert gather, "peer-mapped outputs are gathered by construction"
+            self.col0 = shard_range(self.N, peers.rank, peers.world, self.unit)[0]
             self.out, self.out_ptrs = peers.buffer((max_tokens, self.N), torch.bfloat16)
 
     @classmethod
     def from_full(cls, packed: torch.Tensor, scale: float, K_orig: int, bias: torch.Tensor | None = None,
                   group=None, act_quant: str | None = None, peers: "PeerGroup | None" = None,
-                  max_tokens: int = 64) -> "ShardedPentaLinear":
+                  max_tokens: int = 64, gather: bool = True, unit: int = 1) -> "ShardedPentaLinear":
         rank, world = dist.get_rank(group), dist.get_world_size(group)
-        lo, hi = shard_range(packed.shape[0], rank, world)
+        lo, hi = shard_range(packed.shape[0], rank, world, unit)
         b = bias[lo:hi].contiguous() if bias is not None else None
-        return cls(packed[lo:hi].contiguous(), scale, K_orig, packed.shape[0], b, group, act_quant, peers, max_tokens)
+        return cls(packed[lo:hi].contiguous(), scale, K_orig, packed.shape[0], b, group, act_quant, peers, max_tokens,
+                   gather, unit)
 
     def forward_local(self, x: torch.Tensor) -> torch.Tensor:
         if self.act_quant == "int8":
@@ -121,8 +156,77 @@ class ShardedPentaLinear(torch.nn.Module):
             self.peers.barrier()
             return self.out[:M].reshape(*lead, self.N)
         y_loc = self.forward_local(x.reshape(-1, x.shape[-1]))
-        y = gather_columns(y_loc, self.N, self.world, self.group)
+        if not self.gather:
+            return y_loc.reshape(*lead, y_loc.shape[-1])
+        y = gather_columns(y_loc, self.N, self.world, self.group, unit=self.unit)
         return y.reshape(*lead, self.N)
+
+
+class RowShardedPentaLinear(torch.nn.Module):
+    """The row-parallel partner of a column-parallel layer (the MLP's down
+    projection after its up projection): the weight's input dimension K is split
+    over the ranks at packed-word boundaries, each rank multiplies its slice of
+    the activations by its slice of the weights into an fp32 partial product,
+    one all-reduce sums the partials, and the bias and the reference's bf16
+    rounding (bf16(acc * gamma), then + bf16(bias)) are applied to the sum.
+    Paired with a ShardedPentaLinear(gather=False) sharded with the same
+    `unit`, the activations never leave their rank: one all-reduce per pair
+    instead of an all-gather per layer.  bf16 activations only."""
+
+    def __init__(self, packed_local: torch.Tensor, scale: float, K_local: int, k0: int, K_orig: int,
+                 bias: torch.Tensor | None = None, group=None):
+        super().__init__()
+        self.register_buffer("packed_w", packed_local)  # (N, words of this rank's K slice)
+        self.scale = float(scale)
+        self.K_local = int(K_local)
+        self.k0 = int(k0)
+        self.K_orig = int(K_orig)
+        self.N = int(packed_local.shape[0])
+        self.bias = bias
+        self.group = group
+        self.world = dist.get_world_size(group)
+
+    @staticmethod
+    def slice_k(packed: torch.Tensor, K_orig: int, rank: int, world: int, unit: int = 40):
+        """Rank `rank`'s K slice [lo, hi) of a packed (N, ceil(K/10)) weight: the
+        words covering it (the last rank keeps the padded final word) and lo, hi."""
+        assert unit % pk._W_PER_INT32 == 0, "K slices must start on packed words"
+        lo, hi = shard_range(K_orig, rank, world, unit)
+        w0 = lo // pk._W_PER_INT32
+        w1 = packed.shape[1] if hi == K_orig else hi // pk._W_PER_INT32
+        local = packed[:, w0:w1].contiguous()
+        if local.is_cuda and local.shape[1] > 0:
+            local = pk.pad_packed(local)
+        return local, lo, hi
+
+    @classmethod
+    def from_full(cls, packed: torch.Tensor, scale: float, K_orig: int, bias: torch.Tensor | None = None,
+                  group=None, unit: int = 40) -> "RowShardedPentaLinear":
+        local, lo, hi = cls.slice_k(packed, K_orig, dist.get_rank(group), dist.get_world_size(group), unit)
+        return cls(local, scale, hi - lo, lo, K_orig, bias, group)
+
+    def forward_local(self, x_local: torch.Tensor) -> torch.Tensor:
+        """This rank's fp32 partial product (M, N) = x_local @ W_slice.T * gamma."""
+        if self.K_local == 0:
+            return torch.zeros(x_local.shape[0], self.N, dtype=torch.float32, device=x_local.device)
+        return pk.penta_linear(x_local.to(torch.bfloat16).contiguous(), self.packed_w, self.scale, self.K_local,
+                               out_dtype=torch.float32)
+
+    def forward(self, x: torch.Tensor, x_is_local: bool = False) -> torch.Tensor:
+        """x: the full (..., K) activations, or with x_is_local=True this rank's
+        (..., K_local) slice (a column-parallel layer's gather=False output)."""
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, x.shape[-1])
+        if not x_is_local:
+            x2 = x2[:, self.k0:self.k0 + self.K_local]
+        assert x2.shape[1] == self.K_local, f"expected {self.K_local} input features on this rank, got {x2.shape[1]}"
+        y = self.forward_local(x2)
+        if self.world > 1:
+            dist.all_reduce(y, group=self.group)
+        yb = y.to(torch.bfloat16)
+        if self.bias is not None:
+            yb = (yb.float() + self.bias.detach().to(device=yb.device, dtype=torch.bfloat16).float()).to(torch.bfloat16)
+        return yb.reshape(*lead, self.N)
 
 
 class PeerGroup:

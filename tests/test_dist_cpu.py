@@ -75,3 +75,75 @@ def test_sharded_layer_gloo_world2(tmp_path):
         assert np.array_equal(d["y"], d["want"])
         assert d["y2"].shape == (1,) + d["want"].shape
         assert np.array_equal(d["y2"][0], d["want"])
+
+
+def test_shard_range_aligned():
+    for N in (1, 39, 40, 250, 1000, 2816, 28672):
+        for world in (1, 2, 3, 4, 8):
+            seen = []
+            for r in range(world):
+                lo, hi = pd.shard_range(N, r, world, 40)
+                assert 0 <= lo <= hi <= N
+                assert (lo % 40 == 0 or lo == N) and (hi % 40 == 0 or hi == N)
+                seen.extend(range(lo, hi))
+            assert seen == list(range(N))
+
+
+def _gelu(a: np.ndarray) -> np.ndarray:
+    return torch.nn.functional.gelu(torch.from_numpy(a.astype(np.float32))).numpy()
+
+
+def _pair_worker(rank, world, port, out_dir):
+    """Up projection sharded by output column without a gather, GELU on the
+    local block, down projection sharded by K with one all-reduce; the local
+    products are the oracle's."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        D, H, M = 130, 250, 3
+        w_up, w_dn = gen_weight(H, D, seed=21).numpy(), gen_weight(D, H, seed=22).numpy()
+        g_up, g_dn = float(orc.absmean_scale(w_up)), float(orc.absmean_scale(w_dn))
+        p_up, _, _ = orc.quantize_pack(w_up, g_up)
+        p_dn, _, _ = orc.quantize_pack(w_dn, g_dn)
+        bias = gen_weight(1, D, seed=23, std=0.5).numpy()[0]
+        x = gen_act(M, D, seed=24).float().numpy()
+
+        up = pd.ShardedPentaLinear.from_full(torch.from_numpy(p_up), g_up, D, gather=False, unit=40)
+        up.forward_local = lambda xx: torch.from_numpy(
+            orc.matmul_f64(xx.float().numpy(), orc.unpack(up.packed_w.numpy(), D), g_up).astype(np.float32))
+        dn = pd.RowShardedPentaLinear.from_full(torch.from_numpy(p_dn), g_dn, H, bias=torch.from_numpy(bias), unit=40)
+        dn.forward_local = lambda xl: torch.from_numpy(
+            orc.matmul_f64(xl.float().numpy(), orc.unpack(dn.packed_w.numpy(), dn.K_local), g_dn).astype(np.float32))
+        lo, hi = pd.shard_range(H, rank, world, 40)
+        h_loc = up(torch.from_numpy(x)).numpy()
+        y = dn(torch.from_numpy(_gelu(h_loc)), x_is_local=True).float().numpy()
+
+        h_full = orc.matmul_f64(x, orc.unpack(p_up, D), g_up).astype(np.float32)
+        a_full = _gelu(h_full)
+        y_full_in = dn(torch.from_numpy(a_full)).float().numpy()  # slices the full input itself
+        acc = orc.matmul_f64(a_full, orc.unpack(p_dn, H), g_dn)
+        np.savez(os.path.join(out_dir, f"p{rank}.npz"), lo=lo, hi=hi, k0=dn.k0, K_local=dn.K_local,
+                 h_loc=h_loc, h_want=h_full[:, lo:hi], y=y, y_full_in=y_full_in,
+                 want=orc.bf16_linear_out(acc.astype(np.float32), bias), pre=acc,
+                 words=np.array(dn.packed_w.numpy()), words_want=p_dn[:, lo // 10:(p_dn.shape[1] if hi == H else hi // 10)])
+    finally:
+        dist.destroy_process_group()
+
+
+def test_column_row_pairing_gloo_world2(tmp_path):
+    from _util import assert_bf16_close
+    world = 2
+    mp.start_processes(_pair_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
+    bounds = []
+    for r in range(world):
+        d = np.load(tmp_path / f"p{r}.npz")
+        # the down projection's K slice is exactly the up projection's column block
+        assert int(d["k0"]) == int(d["lo"]) and int(d["K_local"]) == int(d["hi"]) - int(d["lo"])
+        assert np.array_equal(d["words"], d["words_want"])
+        assert np.array_equal(d["h_loc"], d["h_want"])
+        # every rank holds the whole all-reduced output, equal whichever way the input came
+        assert np.array_equal(d["y"], d["y_full_in"])
+        assert_bf16_close(d["y"], d["want"].astype(np.float64), "row-parallel down projection", pre_bias=d["pre"])
+        bounds.append((int(d["lo"]), int(d["hi"])))
+    assert bounds == [(0, 160), (160, 250)]
