@@ -96,6 +96,69 @@ def gather_columns(y_local: torch.Tensor, N: int, world: int, group=None,
     return out
 
 
+SHARD_ROWS, SHARD_K = 0, 1
+
+
+def _register_shard_state(m: torch.nn.Module, scale: float, K_orig: int, axis: int, lo: int, hi: int, full: int,
+                          world: int, unit: int) -> None:
+    """Persist what the packed words alone do not say: gamma, K_orig and which
+    slice of which layout this rank holds ([axis, lo, hi, full, world, unit];
+    axis SHARD_ROWS = output rows [lo, hi) of `full`, SHARD_K = inputs [lo, hi)
+    of K_orig = `full`)."""
+    m.register_buffer("scale_buf", torch.tensor(float(scale), dtype=torch.float32))
+    m.register_buffer("k_orig_buf", torch.tensor(int(K_orig), dtype=torch.int64))
+    m.register_buffer("shard_buf", torch.tensor([axis, lo, hi, full, world, unit], dtype=torch.int64))
+
+
+def _describe_shard(info) -> str:
+    axis, lo, hi, full, world, unit = (int(v) for v in info)
+    what = "output rows" if axis == SHARD_ROWS else "inputs"
+    return f"{what} [{lo}, {hi}) of {full} (world {world}, unit {unit})"
+
+
+def _check_shard_state(m: torch.nn.Module, state_dict, prefix: str) -> None:
+    key = prefix + "shard_buf"
+    if key in state_dict:
+        got, own = state_dict[key].tolist(), m.shard_buf.tolist()
+        assert got == own, (f"checkpoint holds {_describe_shard(got)}, this layer is "
+                            f"{_describe_shard(own)}")
+
+
+def _restore_attrs(m: torch.nn.Module) -> None:
+    m.scale = float(m.scale_buf)
+    m.K_orig = int(m.k_orig_buf)
+
+
+def merge_shards(states: list[dict], prefix: str = "") -> dict:
+    """The unsharded layer's state (PentaLinearFast's keys: the canonical
+    (N, ceil(K/10)) `packed_w`, `scale_buf`, `k_orig_buf` and `bias` when the
+    layer has one) from the state_dicts of every rank's shard of one layer,
+    given in any order.  Output-row shards concatenate by rows; K shards by
+    packed words (their boundaries are word-aligned and the last one holds the
+    padded final word)."""
+    infos = [[int(v) for v in st[prefix + "shard_buf"].tolist()] for st in states]
+    axis, _, _, full, world, unit = infos[0]
+    assert len(states) == world, f"{len(states)} shards for a world of {world}"
+    assert all(i[0] == axis and i[3] == full and i[4] == world and i[5] == unit for i in infos),         "shards of different layouts"
+    order = sorted(range(world), key=lambda r: (infos[r][1], infos[r][2]))
+    assert [(infos[r][1], infos[r][2]) for r in order] == [shard_range(full, r, world, unit) for r in range(world)],         "the shards do not tile the layer (missing or repeated ranks)"
+    scales = {float(st[prefix + "scale_buf"]) for st in states}
+    assert len(scales) == 1, "shards of one layer disagree on gamma"
+    parts = [states[r][prefix + "packed_w"].contiguous() for r in order]
+    out = {"scale_buf": states[0][prefix + "scale_buf"].clone(), "k_orig_buf": states[0][prefix + "k_orig_buf"].clone()}
+    has_bias = prefix + "bias" in states[0]
+    if axis == SHARD_ROWS:
+        out["packed_w"] = torch.cat(parts, dim=0)
+        if has_bias:
+            out["bias"] = torch.cat([states[r][prefix + "bias"] for r in order])
+    else:
+        out["packed_w"] = torch.cat(parts, dim=1)
+        if has_bias:
+            out["bias"] = states[0][prefix + "bias"].clone()
+    assert out["packed_w"].shape[1] == pk._k_packs(int(out["k_orig_buf"])), "merged words do not cover K_orig"
+    return out
+
+
 class ShardedPentaLinear(torch.nn.Module):
     """PentaLinearFast split by output rows over the ranks of `group`; forward
     returns the full (..., N) output on every rank, or with gather=False this
@@ -115,7 +178,10 @@ class ShardedPentaLinear(torch.nn.Module):
         self.group = group
         self.world = dist.get_world_size(group)
         self.act_quant = act_quant
-        self.bias = bias_local
+        self.register_buffer("bias", bias_local)
+        lo, hi = shard_range(self.N, dist.get_rank(group), self.world, self.unit)
+        assert packed_local.shape[0] == hi - lo, f"this rank owns {hi - lo} rows, got {packed_local.shape[0]}"
+        _register_shard_state(self, self.scale, self.K_orig, SHARD_ROWS, lo, hi, self.N, self.world, self.unit)
         # Fused mode: outputs stored into every rank's buffer by the GEMM
         # itself (bf16 activations); the returned tensor is a view of that
         # buffer and is overwritten by the next forward of this layer.
@@ -134,6 +200,11 @@ class ShardedPentaLinear(torch.nn.Module):
         b = bias[lo:hi].contiguous() if bias is not None else None
         return cls(packed[lo:hi].contiguous(), scale, K_orig, packed.shape[0], b, group, act_quant, peers, max_tokens,
                    gather, unit)
+
+    def _load_from_state_dict(self, state_dict, prefix, *args, **kwargs):
+        _check_shard_state(self, state_dict, prefix)
+        super()._load_from_state_dict(state_dict, prefix, *args, **kwargs)
+        _restore_attrs(self)
 
     def forward_local(self, x: torch.Tensor) -> torch.Tensor:
         if self.act_quant == "int8":
@@ -174,7 +245,7 @@ class RowShardedPentaLinear(torch.nn.Module):
     instead of an all-gather per layer.  bf16 activations only."""
 
     def __init__(self, packed_local: torch.Tensor, scale: float, K_local: int, k0: int, K_orig: int,
-                 bias: torch.Tensor | None = None, group=None):
+                 bias: torch.Tensor | None = None, group=None, unit: int = 40):
         super().__init__()
         self.register_buffer("packed_w", packed_local)  # (N, words of this rank's K slice)
         self.scale = float(scale)
@@ -182,9 +253,11 @@ class RowShardedPentaLinear(torch.nn.Module):
         self.k0 = int(k0)
         self.K_orig = int(K_orig)
         self.N = int(packed_local.shape[0])
-        self.bias = bias
+        self.register_buffer("bias", bias)
         self.group = group
         self.world = dist.get_world_size(group)
+        _register_shard_state(self, self.scale, self.K_orig, SHARD_K, self.k0, self.k0 + self.K_local, self.K_orig,
+                              self.world, unit)
 
     @staticmethod
     def slice_k(packed: torch.Tensor, K_orig: int, rank: int, world: int, unit: int = 40):
@@ -194,6 +267,8 @@ class RowShardedPentaLinear(torch.nn.Module):
         lo, hi = shard_range(K_orig, rank, world, unit)
         w0 = lo // pk._W_PER_INT32
         w1 = packed.shape[1] if hi == K_orig else hi // pk._W_PER_INT32
+        if lo == hi:  # a trailing rank without columns holds no words
+            w0 = w1 = 0
         local = packed[:, w0:w1].contiguous()
         if local.is_cuda and local.shape[1] > 0:
             local = pk.pad_packed(local)
@@ -203,7 +278,12 @@ class RowShardedPentaLinear(torch.nn.Module):
     def from_full(cls, packed: torch.Tensor, scale: float, K_orig: int, bias: torch.Tensor | None = None,
                   group=None, unit: int = 40) -> "RowShardedPentaLinear":
         local, lo, hi = cls.slice_k(packed, K_orig, dist.get_rank(group), dist.get_world_size(group), unit)
-        return cls(local, scale, hi - lo, lo, K_orig, bias, group)
+        return cls(local, scale, hi - lo, lo, K_orig, bias, group, unit)
+
+    def _load_from_state_dict(self, state_dict, prefix, *args, **kwargs):
+        _check_shard_state(self, state_dict, prefix)
+        super()._load_from_state_dict(state_dict, prefix, *args, **kwargs)
+        _restore_attrs(self)
 
     def forward_local(self, x_local: torch.Tensor) -> torch.Tensor:
         """This rank's fp32 partial product (M, N) = x_local @ W_slice.T * gamma."""

@@ -90,6 +90,15 @@ class PentaLinearFast(nn.Module):
         bias = layer.bias.detach().clone() if getattr(layer, 'bias', None) is not None else None
         return cls(packed, scale, K_orig, bias, act_quant=act_quant)
 
+    @classmethod
+    def from_state_dict(cls, state: dict, prefix: str = '', act_quant: str | None = None) -> 'PentaLinearFast':
+        """A layer built from a saved PentaLinearFast state_dict (or the merged
+        state of a sharded layer, penta_dist.merge_shards): packed words,
+        gamma, K_orig and bias all come from the state."""
+        bias = state.get(prefix + 'bias')
+        return cls(state[prefix + 'packed_w'].contiguous(), float(state[prefix + 'scale_buf']),
+                   int(state[prefix + 'k_orig_buf']), bias.clone() if bias is not None else None, act_quant=act_quant)
+
     def _pad_weights(self) -> None:
         # Resident CUDA weights are kept at a 16-byte row stride (same shape and
         # values; see penta_kernel.pad_packed) so that the GEMM reads them in

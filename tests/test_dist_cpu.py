@@ -147,3 +147,81 @@ def test_column_row_pairing_gloo_world2(tmp_path):
         assert_bf16_close(d["y"], d["want"].astype(np.float64), "row-parallel down projection", pre_bias=d["pre"])
         bounds.append((int(d["lo"]), int(d["hi"])))
     assert bounds == [(0, 160), (160, 250)]
+
+
+def test_k_slices_concatenate_to_packed():
+    """K slices of every rank, empty trailing ones included, put back together
+    word by word give the packed tensor."""
+    for K in (250, 1000, 1376, 41, 7):
+        packed, _, _ = orc.quantize_pack(gen_weight(5, K, seed=K).numpy())
+        pt = torch.from_numpy(packed)
+        for world in (1, 2, 3, 8):
+            parts = []
+            for r in range(world):
+                local, lo, hi = pd.RowShardedPentaLinear.slice_k(pt, K, r, world)
+                assert local.shape[1] == (0 if lo == hi else orc.k_packs(hi) - lo // 10)
+                parts.append(local)
+            assert torch.equal(torch.cat(parts, dim=1), pt)
+
+
+def _ckpt_worker(rank, world, port, out_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        N, K = 90, 250
+        w = gen_weight(N, K, seed=41).numpy()
+        g = float(orc.absmean_scale(w))
+        packed = torch.from_numpy(orc.quantize_pack(w, g)[0])
+        bias = gen_weight(1, N, seed=42, std=0.5)[0]
+        rows = pd.ShardedPentaLinear.from_full(packed, g, K, bias=bias, unit=40)
+        ks = pd.RowShardedPentaLinear.from_full(packed, g, K, bias=bias, unit=40)
+        torch.save({"rows": rows.state_dict(), "k": ks.state_dict()}, os.path.join(out_dir, f"c{rank}.pt"))
+        dist.barrier()
+        other = torch.load(os.path.join(out_dir, f"c{1 - rank}.pt"))
+        mine = torch.load(os.path.join(out_dir, f"c{rank}.pt"))
+        refused = []
+        for name, layer in (("rows", rows), ("k", ks)):
+            try:
+                layer.load_state_dict(other[name])
+                refused.append(False)
+            except AssertionError:
+                refused.append(True)
+        # a layer built with a wrong gamma takes gamma and K_orig back from its own shard
+        fresh = pd.RowShardedPentaLinear.from_full(packed, 1.0, K, bias=torch.zeros(N), unit=40)
+        fresh.load_state_dict(mine["k"])
+        np.savez(os.path.join(out_dir, f"s{rank}.npz"), refused=np.array(refused), scale=fresh.scale, g=g,
+                 bias_ok=bool(torch.equal(fresh.bias, bias)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_checkpoint_gloo_world2(tmp_path):
+    """Shard info persists: each rank's state_dict names its slice, loading a
+    neighbour's shard is refused, and the shards of either layout merge back
+    into the unsharded layer's packed words, gamma, K_orig and bias."""
+    import pentanet_layer as pl
+    world = 2
+    mp.start_processes(_ckpt_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
+    N, K = 90, 250
+    w = gen_weight(N, K, seed=41).numpy()
+    g = float(orc.absmean_scale(w))
+    packed = torch.from_numpy(orc.quantize_pack(w, g)[0])
+    bias = gen_weight(1, N, seed=42, std=0.5)[0]
+    states = [torch.load(tmp_path / f"c{r}.pt") for r in range(world)]
+    assert states[0]["rows"]["shard_buf"].tolist() == [pd.SHARD_ROWS, 0, 80, N, 2, 40]
+    assert states[1]["k"]["shard_buf"].tolist() == [pd.SHARD_K, 160, 250, K, 2, 40]
+    for name in ("rows", "k"):
+        for order in ([0, 1], [1, 0]):
+            merged = pd.merge_shards([states[r][name] for r in order])
+            assert torch.equal(merged["packed_w"], packed)
+            assert float(merged["scale_buf"]) == np.float32(g) and int(merged["k_orig_buf"]) == K
+            assert torch.equal(merged["bias"], bias)
+        with pytest.raises(AssertionError):
+            pd.merge_shards([states[0][name], states[0][name]])
+        fast = pl.PentaLinearFast.from_state_dict(pd.merge_shards([s[name] for s in states]))
+        assert torch.equal(fast.packed_w, packed) and fast.K_orig == K and fast.scale == float(np.float32(g))
+    for r in range(world):
+        d = np.load(tmp_path / f"s{r}.npz")
+        assert d["refused"].all()
+        assert float(d["scale"]) == float(np.float32(d["g"])) and bool(d["bias_ok"])
