@@ -38,6 +38,9 @@ enum pn_status_code {
 /* ---- element types -------------------------------------------------------- */
 enum pn_dtype { PN_F32 = 0, PN_BF16 = 1, PN_I8 = 2, PN_I32 = 3 };
 
+/* Activation fused into a product's epilogue (pn_linear_bf16_epi / _i8_epi). */
+enum pn_act_code { PN_ACT_NONE = 0, PN_ACT_GELU = 1 };
+
 /* ABI version of this header (bumped on any signature change). */
 int pn_abi_version(void);
 /* Static text for a status code. */
@@ -122,6 +125,22 @@ int pn_linear_bf16_ld(const void *x, int64_t M, int64_t K, const int32_t *packed
                       int64_t packed_ld, float scale, const void *bias, void *y, int y_dtype, void *workspace,
                       size_t workspace_bytes, void *stream);
 
+/* pn_linear_bf16_ld with the elementwise ops that follow a projection in the
+ * reference's GPT block fused into the epilogue, each rounded to bf16 as the
+ * separate torch ops round it (fp32 output: no intermediate rounding):
+ *   t = bf16(acc * scale); t = bf16(t + bf16(bias))       (bias != NULL)
+ *   t = bf16(gelu(t))      (act == PN_ACT_GELU; erf form, nn.GELU(),
+ *                           train_pentagpt.py:80,86)
+ *   y = bf16(residual + t) (residual != NULL; x + attn(..) / x + mlp(..),
+ *                           train_pentagpt.py:100-101)
+ * residual: NULL or (M, ld_res) bf16, ld_res >= N; it may be y itself (then
+ * ld_res == N), each element being read before its output is written.  No
+ * reference counterpart: the reference runs these as separate torch ops. */
+int pn_linear_bf16_epi(const void *x, int64_t M, int64_t K, const int32_t *packed, int64_t N, int64_t K_packs,
+                       int64_t packed_ld, float scale, const void *bias, int act, const void *residual,
+                       int64_t ld_res, void *y, int y_dtype, void *workspace, size_t workspace_bytes,
+                       void *stream);
+
 /* The packed row stride (int32 words) that lets the GEMM read weights in
  * place: K_packs rounded up to a multiple of 4. */
 int64_t pn_packed_ld(int64_t K_packs);
@@ -166,6 +185,13 @@ int pn_linear_i8_ld(const int8_t *xq, int64_t xq_pitch, const float *s_x, const 
                     int64_t K, const int32_t *packed, int64_t N, int64_t K_packs, int64_t packed_ld, float scale,
                     const void *bias, void *y, int y_dtype, int32_t *acc_out, void *workspace,
                     size_t workspace_bytes, void *stream);
+
+/* pn_linear_i8_ld with the fused epilogue ops of pn_linear_bf16_epi (y must
+ * not be NULL when act or residual is given). */
+int pn_linear_i8_epi(const int8_t *xq, int64_t xq_pitch, const float *s_x, const int32_t *rowsum, int64_t M,
+                     int64_t K, const int32_t *packed, int64_t N, int64_t K_packs, int64_t packed_ld, float scale,
+                     const void *bias, int act, const void *residual, int64_t ld_res, void *y, int y_dtype,
+                     int32_t *acc_out, void *workspace, size_t workspace_bytes, void *stream);
 
 /* Number of SMs of the current device (used to size launches and shards). */
 int pn_device_sm_count(int *count_out);

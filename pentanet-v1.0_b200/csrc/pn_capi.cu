@@ -53,6 +53,19 @@ bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 
 int64_t k_packs(int64_t K) { return (K + pn::kPerWord - 1) / pn::kPerWord; }
 
+// Fused epilogue arguments shared by the bf16 and int8 products.
+int check_epilogue(const void* residual, int64_t ld_res, int act, int64_t N, const void* y, int n_peers,
+                   const char* name) {
+    if (act != PN_ACT_NONE && act != PN_ACT_GELU) return fail(PN_ERR_ARG, "%s: act %d", name, act);
+    if (!residual) return PN_OK;
+    if (n_peers > 0) return fail(PN_ERR_UNSUPPORTED, "%s: no residual for output-sharded products", name);
+    if (ld_res < N) return fail(PN_ERR_SHAPE, "%s: ld_res=%lld < N=%lld", name, (long long)ld_res, (long long)N);
+    if (residual == y && ld_res != N)
+        return fail(PN_ERR_SHAPE, "%s: an in-place residual needs ld_res == N", name);
+    if (!aligned(residual, 2)) return fail(PN_ERR_ALIGN, "%s: misaligned residual", name);
+    return PN_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -164,9 +177,9 @@ size_t pn_linear_workspace_min_size(int kind, int64_t M, int64_t N, int64_t K) {
 namespace {
 // pn_linear_bf16 and its output-sharded form share validation and launch.
 int linear_bf16_impl(const void* x, int64_t M, int64_t K, const int32_t* packed, int64_t N, int64_t K_packs,
-                     int64_t packed_ld, float scale, const void* bias, void* y, int y_dtype, void* workspace,
-                     size_t workspace_bytes, void* stream, void* const* y_peers, int n_peers, int64_t ld_y,
-                     int64_t y_col0, const char* name) {
+                     int64_t packed_ld, float scale, const void* bias, const void* residual, int64_t ld_res, int act,
+                     void* y, int y_dtype, void* workspace, size_t workspace_bytes, void* stream,
+                     void* const* y_peers, int n_peers, int64_t ld_y, int64_t y_col0, const char* name) {
     if ((!x && M > 0) || (!packed && N > 0) || (!y && n_peers == 0 && M > 0 && N > 0))
         return fail(PN_ERR_ARG, "%s: null pointer", name);
     if (y_dtype != PN_BF16 && y_dtype != PN_F32) return fail(PN_ERR_DTYPE, "%s: y_dtype %d", name, y_dtype);
@@ -179,6 +192,7 @@ int linear_bf16_impl(const void* x, int64_t M, int64_t K, const int32_t* packed,
         return fail(PN_ERR_SHAPE, "%s: packed_ld=%lld < K_packs=%lld", name, (long long)packed_ld, (long long)K_packs);
     if (!aligned(x, 2) || !aligned(packed, 16) || !aligned(y, y_dtype == PN_F32 ? 4 : 2) || !aligned(bias, 2))
         return fail(PN_ERR_ALIGN, "%s: misaligned pointer (packed weights need 16-byte alignment)", name);
+    if (int st = check_epilogue(residual, ld_res, act, N, y, n_peers, name)) return st;
     const size_t need = pn::linear_workspace_min_bytes(PN_BF16, M, N, K);
     if (need > 0 && (!workspace || workspace_bytes < need))
         return fail(PN_ERR_WORKSPACE, "%s: workspace needs at least %zu bytes (%zu recommended)", name, need,
@@ -197,6 +211,9 @@ int linear_bf16_impl(const void* x, int64_t M, int64_t K, const int32_t* packed,
     a.packed_ld = packed_ld;
     a.scale = scale;
     a.bias = bias;
+    a.residual = residual;
+    a.ld_res = ld_res;
+    a.act = act;
     a.y = y;
     a.y_dtype = y_dtype;
     a.workspace = workspace;
@@ -225,8 +242,8 @@ extern "C" {
 int pn_linear_bf16(const void* x, int64_t M, int64_t K, const int32_t* packed, int64_t N, int64_t K_packs,
                    float scale, const void* bias, void* y, int y_dtype, void* workspace, size_t workspace_bytes,
                    void* stream) {
-    return linear_bf16_impl(x, M, K, packed, N, K_packs, K_packs, scale, bias, y, y_dtype, workspace, workspace_bytes,
-                            stream, nullptr, 0, 0, 0, "pn_linear_bf16");
+    return linear_bf16_impl(x, M, K, packed, N, K_packs, K_packs, scale, bias, nullptr, 0, PN_ACT_NONE, y, y_dtype,
+                            workspace, workspace_bytes, stream, nullptr, 0, 0, 0, "pn_linear_bf16");
 }
 
 int64_t pn_packed_ld(int64_t K_packs) { return K_packs <= 0 ? 0 : (K_packs + 3) / 4 * 4; }
@@ -234,8 +251,15 @@ int64_t pn_packed_ld(int64_t K_packs) { return K_packs <= 0 ? 0 : (K_packs + 3) 
 int pn_linear_bf16_ld(const void* x, int64_t M, int64_t K, const int32_t* packed, int64_t N, int64_t K_packs,
                       int64_t packed_ld, float scale, const void* bias, void* y, int y_dtype, void* workspace,
                       size_t workspace_bytes, void* stream) {
-    return linear_bf16_impl(x, M, K, packed, N, K_packs, packed_ld, scale, bias, y, y_dtype, workspace,
-                            workspace_bytes, stream, nullptr, 0, 0, 0, "pn_linear_bf16_ld");
+    return linear_bf16_impl(x, M, K, packed, N, K_packs, packed_ld, scale, bias, nullptr, 0, PN_ACT_NONE, y, y_dtype,
+                            workspace, workspace_bytes, stream, nullptr, 0, 0, 0, "pn_linear_bf16_ld");
+}
+
+int pn_linear_bf16_epi(const void* x, int64_t M, int64_t K, const int32_t* packed, int64_t N, int64_t K_packs,
+                       int64_t packed_ld, float scale, const void* bias, int act, const void* residual,
+                       int64_t ld_res, void* y, int y_dtype, void* workspace, size_t workspace_bytes, void* stream) {
+    return linear_bf16_impl(x, M, K, packed, N, K_packs, packed_ld, scale, bias, residual, ld_res, act, y, y_dtype,
+                            workspace, workspace_bytes, stream, nullptr, 0, 0, 0, "pn_linear_bf16_epi");
 }
 
 int64_t pn_act_i8_pitch(int64_t K) { return pn::act_i8_pitch(K); }
@@ -256,8 +280,8 @@ int pn_quant_act_i8(const void* x, int x_dtype, int64_t M, int64_t K, int8_t* xq
 
 static int linear_i8_impl(const int8_t* xq, int64_t xq_pitch, const float* s_x, const int32_t* rowsum, int64_t M,
                           int64_t K, const int32_t* packed, int64_t N, int64_t K_packs, int64_t packed_ld, float scale,
-                          const void* bias, void* y, int y_dtype, int32_t* acc_out, void* workspace,
-                          size_t workspace_bytes, void* stream) {
+                          const void* bias, const void* residual, int64_t ld_res, int act, void* y, int y_dtype,
+                          int32_t* acc_out, void* workspace, size_t workspace_bytes, void* stream) {
     if (M > 0 && N > 0 && (!xq || !s_x || !rowsum || !packed || (!y && !acc_out)))
         return fail(PN_ERR_ARG, "pn_linear_i8: null pointer");
     if (y && y_dtype != PN_BF16 && y_dtype != PN_F32) return fail(PN_ERR_DTYPE, "pn_linear_i8: y_dtype %d", y_dtype);
@@ -273,6 +297,8 @@ static int linear_i8_impl(const int8_t* xq, int64_t xq_pitch, const float* s_x, 
     if (!aligned(xq, 16) || !aligned(packed, 16) || !aligned(s_x, 4) || !aligned(rowsum, 4) || !aligned(acc_out, 4) ||
         !aligned(y, y_dtype == PN_F32 ? 4 : 2) || !aligned(bias, 2))
         return fail(PN_ERR_ALIGN, "pn_linear_i8: misaligned pointer");
+    if ((residual || act != PN_ACT_NONE) && !y) return fail(PN_ERR_ARG, "pn_linear_i8: epilogue ops need y");
+    if (int st = check_epilogue(residual, ld_res, act, N, y, 0, "pn_linear_i8")) return st;
     const size_t need = pn::linear_workspace_min_bytes(PN_I8, M, N, K);
     if (need > 0 && (!workspace || workspace_bytes < need))
         return fail(PN_ERR_WORKSPACE, "pn_linear_i8: workspace needs at least %zu bytes (%zu recommended)", need,
@@ -291,6 +317,9 @@ static int linear_i8_impl(const int8_t* xq, int64_t xq_pitch, const float* s_x, 
     a.packed_ld = packed_ld;
     a.scale = scale;
     a.bias = bias;
+    a.residual = residual;
+    a.ld_res = ld_res;
+    a.act = act;
     a.y = y;
     a.y_dtype = y_dtype;
     a.acc_out = acc_out;
@@ -309,16 +338,24 @@ static int linear_i8_impl(const int8_t* xq, int64_t xq_pitch, const float* s_x, 
 int pn_linear_i8(const int8_t* xq, int64_t xq_pitch, const float* s_x, const int32_t* rowsum, int64_t M, int64_t K,
                  const int32_t* packed, int64_t N, int64_t K_packs, float scale, const void* bias, void* y,
                  int y_dtype, int32_t* acc_out, void* workspace, size_t workspace_bytes, void* stream) {
-    return linear_i8_impl(xq, xq_pitch, s_x, rowsum, M, K, packed, N, K_packs, K_packs, scale, bias, y, y_dtype,
-                          acc_out, workspace, workspace_bytes, stream);
+    return linear_i8_impl(xq, xq_pitch, s_x, rowsum, M, K, packed, N, K_packs, K_packs, scale, bias, nullptr, 0,
+                          PN_ACT_NONE, y, y_dtype, acc_out, workspace, workspace_bytes, stream);
 }
 
 int pn_linear_i8_ld(const int8_t* xq, int64_t xq_pitch, const float* s_x, const int32_t* rowsum, int64_t M,
                     int64_t K, const int32_t* packed, int64_t N, int64_t K_packs, int64_t packed_ld, float scale,
                     const void* bias, void* y, int y_dtype, int32_t* acc_out, void* workspace,
                     size_t workspace_bytes, void* stream) {
-    return linear_i8_impl(xq, xq_pitch, s_x, rowsum, M, K, packed, N, K_packs, packed_ld, scale, bias, y, y_dtype,
-                          acc_out, workspace, workspace_bytes, stream);
+    return linear_i8_impl(xq, xq_pitch, s_x, rowsum, M, K, packed, N, K_packs, packed_ld, scale, bias, nullptr, 0,
+                          PN_ACT_NONE, y, y_dtype, acc_out, workspace, workspace_bytes, stream);
+}
+
+int pn_linear_i8_epi(const int8_t* xq, int64_t xq_pitch, const float* s_x, const int32_t* rowsum, int64_t M,
+                     int64_t K, const int32_t* packed, int64_t N, int64_t K_packs, int64_t packed_ld, float scale,
+                     const void* bias, int act, const void* residual, int64_t ld_res, void* y, int y_dtype,
+                     int32_t* acc_out, void* workspace, size_t workspace_bytes, void* stream) {
+    return linear_i8_impl(xq, xq_pitch, s_x, rowsum, M, K, packed, N, K_packs, packed_ld, scale, bias, residual, ld_res,
+                          act, y, y_dtype, acc_out, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

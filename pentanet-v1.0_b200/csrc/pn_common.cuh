@@ -22,6 +22,38 @@ constexpr uint32_t kZeroWord = 0x12492492u;
 // reason here (first writer wins); the host reads it with pn_device_status().
 __device__ int g_device_status = 0;
 
+// Epilogue activations (pn_act_code in the C header).
+constexpr int kActNone = 0;
+constexpr int kActGelu = 1;
+
+// GELU, erf form, in fp32 with torch's operation order for bf16 tensors
+// (x * 0.5 * (1 + erf(x * sqrt(1/2))), the approximate='none' nn.GELU of the
+// GPT's MLP, train_pentagpt.py:80,86); erff is CUDA's.
+__device__ __forceinline__ float gelu_erf(float v) {
+    return __fmul_rn(__fmul_rn(v, 0.5f), __fadd_rn(1.0f, erff(__fmul_rn(v, 0.7071067811865476f))));
+}
+
+// The epilogue after the product's bf16 rounding, in the order the reference
+// model applies the separate ops: + bias (bf16(t + bf16 bias),
+// penta_kernel.py:275-276), the activation (bf16(gelu(t))), then the residual
+// stream (bf16(res + t), train_pentagpt.py:100-101).
+__device__ __forceinline__ __nv_bfloat16 epilogue_bf16(float yv, const __nv_bfloat16* bias_n, float bias_f, int act,
+                                                       const __nv_bfloat16* res) {
+    __nv_bfloat16 t = __float2bfloat16_rn(yv);
+    if (bias_n) t = __float2bfloat16_rn(__fadd_rn(__bfloat162float(t), bias_f));
+    if (act == kActGelu) t = __float2bfloat16_rn(gelu_erf(__bfloat162float(t)));
+    if (res) t = __float2bfloat16_rn(__fadd_rn(__bfloat162float(*res), __bfloat162float(t)));
+    return t;
+}
+// The fp32-output form: no intermediate rounding.
+__device__ __forceinline__ float epilogue_f32(float yv, const __nv_bfloat16* bias_n, float bias_f, int act,
+                                             const __nv_bfloat16* res) {
+    if (bias_n) yv = __fadd_rn(yv, bias_f);
+    if (act == kActGelu) yv = gelu_erf(yv);
+    if (res) yv = __fadd_rn(__bfloat162float(*res), yv);
+    return yv;
+}
+
 __device__ __forceinline__ void record_status(int code) {
     atomicCAS(&g_device_status, 0, code);
 }

@@ -146,6 +146,9 @@ struct DqmmParams {
     const uint8_t* xperm;  // permuted activation slabs (bf16 decode tiles)
     float scale;
     const __nv_bfloat16* bias;
+    const __nv_bfloat16* residual;  // (M, ld_res) bf16 added after the activation, or null
+    int64_t ld_res;
+    int act;               // kActNone / kActGelu
     void* y_out[8];        // output buffers (one, or one per GPU of an output-sharded layer)
     int n_out;
     int64_t ld_y, y_col0;  // row stride of the outputs and this shard's first column
@@ -297,7 +300,11 @@ __device__ __forceinline__ void red_add(int* p, int v) {
     asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-template <Kind KIND, int BT>
+// EPI: the instance that also fuses an activation and a residual add into
+// the epilogue (separate instances keep the plain products' register
+// allocation untouched; the extra epilogue code costs registers at the
+// 80-per-thread budget).
+template <Kind KIND, int BT, bool EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     dqmm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmap_tail,
                 const __grid_constant__ CUtensorMap wmap, const DqmmParams p) {
@@ -641,8 +648,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         yv = __fmul_rn((float)acc_i, f);
                     }
                     if (p.n_out > 0) {
+                        const __nv_bfloat16* res = nullptr;
+                        int act = kActNone;
+                        if constexpr (EPI) {
+                            if (p.residual) res = p.residual + (int64_t)m * p.ld_res + n;
+                            act = p.act;
+                        }
                         if (p.y_f32) {
-                            if (p.bias) yv = __fadd_rn(yv, bias_f);
+                            yv = epilogue_f32(yv, p.bias, bias_f, act, res);
                             if constexpr (MULTI) {
                                 const int64_t off = (int64_t)m * p.ld_y + p.y_col0 + n;
                                 for (int r = 0; r < p.n_out; ++r) static_cast<float*>(p.y_out[r])[off] = yv;
@@ -650,8 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 y0f[(int64_t)m * p.N + n] = yv;
                             }
                         } else {
-                            __nv_bfloat16 t = __float2bfloat16_rn(yv);
-                            if (p.bias) t = __float2bfloat16_rn(__fadd_rn(__bfloat162float(t), bias_f));
+                            const __nv_bfloat16 t = epilogue_bf16(yv, p.bias, bias_f, act, res);
                             if constexpr (MULTI) {
                                 const int64_t off = (int64_t)m * p.ld_y + p.y_col0 + n;
                                 for (int r = 0; r < p.n_out; ++r) static_cast<__nv_bfloat16*>(p.y_out[r])[off] = t;
@@ -704,9 +716,49 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < 16; ++j) yp[(int64_t)j * p.ld_y] = v[j];
                 }
             };
-            const bool plain_out = !p.y_f32 && p.bias == nullptr && p.acc_out == nullptr;
+            // One bf16 output with a bias, an activation or a residual: the
+            // same straight pass with the fused epilogue ops.
+            auto finish_epi = [&](int c0, const uint32_t (&acc)[16]) {
+                if (n >= p.N) return;
+                __nv_bfloat16* yp = y0h + (int64_t)(m0 + c0) * p.N + n;
+                const __nv_bfloat16* rp = p.residual + (int64_t)(m0 + c0) * p.ld_res + n;
+                // Residual values are loaded eight at a time ahead of their
+                // stores: the residual may be the output itself, so the compiler
+                // cannot move a load above an earlier store, and interleaved they
+                // would cost one memory round trip per value.
+#pragma unroll
+                for (int j0 = 0; j0 < 16; j0 += 8) {
+                    __nv_bfloat16 rv[8];
+                    if (p.residual) {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) rv[j] = rp[(int64_t)(j0 + j) * p.ld_res];
+                    }
+#pragma unroll
+                    for (int j = j0; j < j0 + 8; ++j) {
+                        float yv;
+                        if constexpr (KIND == Kind::F16) {
+                            yv = __fmul_rn(__uint_as_float(acc[j]), p.scale);
+                        } else {
+                            const int m = m0 + c0 + j;
+                            const int acc_i = (int)acc[j] - 2 * __ldg(p.rowsum + m);
+                            yv = __fmul_rn((float)acc_i, __fmul_rn(p.scale, __ldg(p.s_x + m)));
+                        }
+                        yp[(int64_t)j * p.N] =
+                            epilogue_bf16(yv, p.bias, bias_f, p.act, p.residual ? &rv[j - j0] : nullptr);
+                    }
+                }
+            };
+            const bool plain_out = !p.y_f32 && p.bias == nullptr && p.acc_out == nullptr &&
+                                   (!EPI || (p.residual == nullptr && p.act == kActNone));
             const bool fast_out = p.n_out == 1 && plain_out;
+            const bool epi_out = EPI && p.n_out == 1 && !p.y_f32 && p.acc_out == nullptr && !plain_out;
             auto finish = [&](int c0, const uint32_t (&acc)[16]) {
+                if constexpr (EPI) {
+                    if (epi_out && m0 + c0 + 16 <= p.M) {
+                        finish_epi(c0, acc);
+                        return;
+                    }
+                }
                 if (fast_out && m0 + c0 + 16 <= p.M)
                     finish_fast(c0, acc);
                 else if (p.n_out > 1 && plain_out && m0 + c0 + 16 <= p.M)
@@ -1013,7 +1065,7 @@ __global__ void __launch_bounds__(256) repitch_kernel(const int32_t* __restrict_
     }
 }
 
-template <Kind KIND, int BT>
+template <Kind KIND, int BT, bool EPI>
 static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, const char** why) {
     using C = Cfg<KIND, BT>;
     using T = typename C::T;
@@ -1160,6 +1212,9 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     }
     prm.scale = a.scale;
     prm.bias = static_cast<const __nv_bfloat16*>(a.bias);
+    prm.residual = static_cast<const __nv_bfloat16*>(a.residual);
+    prm.ld_res = a.ld_res;
+    prm.act = a.act;
     if (a.n_peers > 0) {
         prm.n_out = a.n_peers;
         for (int r = 0; r < 8; ++r) prm.y_out[r] = r < a.n_peers ? a.y_peers[r] : nullptr;
@@ -1176,7 +1231,7 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     prm.s_x = a.s_x;
     prm.rowsum = a.rowsum;
 
-    auto kern = dqmm_kernel<KIND, BT>;
+    auto kern = dqmm_kernel<KIND, BT, EPI>;
     static bool attr_done[64] = {};  // per instantiation and device
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1218,17 +1273,17 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     return PN_OK;
 }
 
-template <Kind KIND>
+template <Kind KIND, bool EPI>
 static int launch_kind(const LinearArgs& a, cudaStream_t s, cudaError_t* err, const char** why) {
-    if (a.M <= 16) return launch_bt<KIND, 16>(a, s, err, why);
-    if (a.M <= 32) return launch_bt<KIND, 32>(a, s, err, why);
-    if (a.M <= 64) return launch_bt<KIND, 64>(a, s, err, why);
+    if (a.M <= 16) return launch_bt<KIND, 16, EPI>(a, s, err, why);
+    if (a.M <= 32) return launch_bt<KIND, 32, EPI>(a, s, err, why);
+    if (a.M <= 64) return launch_bt<KIND, 64, EPI>(a, s, err, why);
     if constexpr (KIND == Kind::F16) {
         // bf16 operands of a 256-token tile leave TMEM room for only 3 operand stages
-        return launch_bt<KIND, 128>(a, s, err, why);
+        return launch_bt<KIND, 128, EPI>(a, s, err, why);
     } else {
-        if (a.M <= 128) return launch_bt<KIND, 128>(a, s, err, why);
-        return launch_bt<KIND, 256>(a, s, err, why);
+        if (a.M <= 128) return launch_bt<KIND, 128, EPI>(a, s, err, why);
+        return launch_bt<KIND, 256, EPI>(a, s, err, why);
     }
 }
 
@@ -1236,8 +1291,10 @@ int launch_linear(const LinearArgs& a, cudaStream_t s, cudaError_t* err, const c
     *err = cudaSuccess;
     *why = "";
     if (a.M == 0 || a.N == 0) return PN_OK;
-    if (a.kind == PN_BF16) return launch_kind<Kind::F16>(a, s, err, why);
-    return launch_kind<Kind::I8>(a, s, err, why);
+    const bool epi = a.act != kActNone || a.residual != nullptr;
+    if (a.kind == PN_BF16)
+        return epi ? launch_kind<Kind::F16, true>(a, s, err, why) : launch_kind<Kind::F16, false>(a, s, err, why);
+    return epi ? launch_kind<Kind::I8, true>(a, s, err, why) : launch_kind<Kind::I8, false>(a, s, err, why);
 }
 
 }  // namespace pn

@@ -26,6 +26,9 @@ struct LinearArgs {
     int64_t packed_ld;        // int32 words between packed rows (>= KP)
     float scale;
     const void* bias;         // bf16 (N) or null
+    const void* residual;     // bf16 (M, ld_res) added after the activation, or null
+    int64_t ld_res;
+    int act;                  // PN_ACT_NONE / PN_ACT_GELU
     void* y;                  // (M, N) or null (int8 path only)
     int y_dtype;              // PN_BF16 / PN_F32
     // Output-sharded layers: when n_peers > 0 the outputs go to every buffer

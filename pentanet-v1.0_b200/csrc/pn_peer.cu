@@ -134,6 +134,7 @@ extern "C" int pn_linear_bf16_peers(const void* x, int64_t M, int64_t K, const i
             return fail(PN_ERR_ALIGN, "pn_linear_bf16_peers: output %d", r);
     if (M > 64 && (K % 8 != 0 || !aligned(x, 16)))
         return fail(PN_ERR_UNSUPPORTED, "pn_linear_bf16_peers: M > 64 needs K %% 8 == 0 and 16-byte aligned x");
-    return linear_bf16_impl(x, M, K, packed, N, K_packs, K_packs, scale, bias, nullptr, y_dtype, workspace,
-                            workspace_bytes, stream, y_peers, n_peers, ld_y, y_col0, "pn_linear_bf16_peers");
+    return linear_bf16_impl(x, M, K, packed, N, K_packs, K_packs, scale, bias, nullptr, 0, PN_ACT_NONE, nullptr,
+                            y_dtype, workspace, workspace_bytes, stream, y_peers, n_peers, ld_y, y_col0,
+                            "pn_linear_bf16_peers");
 }

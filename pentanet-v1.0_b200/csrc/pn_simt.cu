@@ -15,6 +15,7 @@ __global__ void __launch_bounds__(256) simt_bf16_kernel(const __nv_bfloat16* __r
                                                         const int32_t* __restrict__ packed, int64_t ld, int64_t N,
                                                         int64_t KP,
                                                         float scale, const __nv_bfloat16* __restrict__ bias,
+                                                        const __nv_bfloat16* residual, int64_t ld_res, int act,
                                                         void* __restrict__ y, int y_f32) {
     const int64_t n = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -45,15 +46,12 @@ __global__ void __launch_bounds__(256) simt_bf16_kernel(const __nv_bfloat16* __r
             for (int j = 0; j < kSimtTok; ++j) {
                 const int64_t m = m0 + j;
                 if (m >= M) break;
-                float yv = __fmul_rn(acc[j], scale);
-                if (y_f32) {
-                    if (bias) yv = __fadd_rn(yv, bias_f);
-                    static_cast<float*>(y)[m * N + n] = yv;
-                } else {
-                    __nv_bfloat16 t = __float2bfloat16_rn(yv);
-                    if (bias) t = __float2bfloat16_rn(__fadd_rn(__bfloat162float(t), bias_f));
-                    static_cast<__nv_bfloat16*>(y)[m * N + n] = t;
-                }
+                const float yv = __fmul_rn(acc[j], scale);
+                const __nv_bfloat16* res = residual ? residual + m * ld_res + n : nullptr;
+                if (y_f32)
+                    static_cast<float*>(y)[m * N + n] = epilogue_f32(yv, bias, bias_f, act, res);
+                else
+                    static_cast<__nv_bfloat16*>(y)[m * N + n] = epilogue_bf16(yv, bias, bias_f, act, res);
             }
         }
     }
@@ -64,8 +62,9 @@ cudaError_t launch_linear_simt_bf16(const LinearArgs& a, cudaStream_t s) {
     const int warps = 8;
     const unsigned blocks = (unsigned)((a.N + warps - 1) / warps);
     simt_bf16_kernel<<<blocks, warps * 32, 0, s>>>(static_cast<const __nv_bfloat16*>(a.x), a.M, a.K, a.packed, a.packed_ld, a.N,
-                                                   a.KP, a.scale, static_cast<const __nv_bfloat16*>(a.bias), a.y,
-                                                   a.y_dtype == PN_F32);
+                                                   a.KP, a.scale, static_cast<const __nv_bfloat16*>(a.bias),
+                                                   static_cast<const __nv_bfloat16*>(a.residual), a.ld_res, a.act,
+                                                   a.y, a.y_dtype == PN_F32);
     return cudaGetLastError();
 }
 

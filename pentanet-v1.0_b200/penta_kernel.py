@@ -180,8 +180,23 @@ def _packed_rows(packed_w: torch.Tensor) -> tuple[torch.Tensor, int]:
 
 # ── Fused dequant-matmul ─────────────────────────────────────────────────────
 
+_ACTS = {None: _nat.PN_ACT_NONE, 'none': _nat.PN_ACT_NONE, 'gelu': _nat.PN_ACT_GELU}
+
+
+def _epilogue_args(act, residual, lead, N, device):
+    """(activation code, residual (M, N) bf16 or None) for the fused epilogue."""
+    assert act in _ACTS, f"act must be one of {sorted(k for k in _ACTS if k)} or None, got {act!r}"
+    if residual is None:
+        return _ACTS[act], None
+    assert residual.dtype == torch.bfloat16, "residual must be bfloat16"
+    assert residual.device == device, "residual must be on the activations' device"
+    assert tuple(residual.shape) == (*lead, N), f"residual shape {tuple(residual.shape)} != {(*lead, N)}"
+    return _ACTS[act], residual.contiguous().reshape(-1, N)
+
+
 def penta_linear(x: torch.Tensor, packed_w: torch.Tensor, scale: float, K_orig: int,
-                 bias: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+                 bias: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
+                 act: str | None = None, residual: torch.Tensor | None = None) -> torch.Tensor:
     """Fast pentanary linear: Y = X @ W.T * scale + bias (penta_kernel.py:229-278).
 
     Args:
@@ -192,6 +207,11 @@ def penta_linear(x: torch.Tensor, packed_w: torch.Tensor, scale: float, K_orig: 
         bias     : (N,) optional bias tensor
         out_dtype: torch.bfloat16 (reference rounding) or torch.float32 (the
                    unrounded fp32 result; not in the reference)
+        act      : None or 'gelu' -- applied in the epilogue after the bias,
+                   rounded as a separate bf16 F.gelu would be (not in the
+                   reference's wrapper; its GPT applies nn.GELU after c_fc)
+        residual : None or a (..., N) bf16 tensor added last, as the GPT
+                   block's `x + proj(..)` (train_pentagpt.py:100-101)
 
     Returns:
         y : (..., N) of out_dtype
@@ -205,6 +225,7 @@ def penta_linear(x: torch.Tensor, packed_w: torch.Tensor, scale: float, K_orig: 
     M, K = x_2d.shape
     N, K_packs = packed_w.shape
     assert K == K_orig, f"Activation K={K} must match K_orig={K_orig}"
+    act_code, res = _epilogue_args(act, residual, orig_shape[:-1], N, x.device)
     pw, ld = _packed_rows(packed_w)
     y = torch.empty(M, N, device=x.device, dtype=out_dtype)
     b = None
@@ -214,10 +235,15 @@ def penta_linear(x: torch.Tensor, packed_w: torch.Tensor, scale: float, K_orig: 
     L = _nat.load()
     ws_bytes = int(L.pn_linear_workspace_size(_nat.PN_BF16, M, N, K))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
-    _nat.check(L.pn_linear_bf16_ld(x_2d.data_ptr(), M, K, pw.data_ptr(), N, K_packs, ld, ctypes.c_float(scale),
-                                   _nat.ptr(b), y.data_ptr(),
-                                   _nat.PN_F32 if out_dtype == torch.float32 else _nat.PN_BF16,
-                                   _nat.ptr(ws), ws_bytes, _nat.stream_of(x_2d)), "penta_linear")
+    ydt = _nat.PN_F32 if out_dtype == torch.float32 else _nat.PN_BF16
+    if act_code == _nat.PN_ACT_NONE and res is None:
+        _nat.check(L.pn_linear_bf16_ld(x_2d.data_ptr(), M, K, pw.data_ptr(), N, K_packs, ld, ctypes.c_float(scale),
+                                       _nat.ptr(b), y.data_ptr(), ydt, _nat.ptr(ws), ws_bytes,
+                                       _nat.stream_of(x_2d)), "penta_linear")
+    else:
+        _nat.check(L.pn_linear_bf16_epi(x_2d.data_ptr(), M, K, pw.data_ptr(), N, K_packs, ld, ctypes.c_float(scale),
+                                        _nat.ptr(b), act_code, _nat.ptr(res), N, y.data_ptr(), ydt, _nat.ptr(ws),
+                                        ws_bytes, _nat.stream_of(x_2d)), "penta_linear")
     return y.reshape(*orig_shape[:-1], N)
 
 
@@ -245,14 +271,18 @@ def quantize_activations_i8(x: torch.Tensor):
 
 def penta_linear_i8_prequant(xq: torch.Tensor, s_x: torch.Tensor, rowsum: torch.Tensor, K_orig: int,
                              packed_w: torch.Tensor, scale: float, bias: torch.Tensor | None = None,
-                             out_dtype: torch.dtype | None = torch.bfloat16, return_acc: bool = False):
+                             out_dtype: torch.dtype | None = torch.bfloat16, return_acc: bool = False,
+                             act: str | None = None, residual: torch.Tensor | None = None):
     """int8 x packed-weight GEMM on already-quantised activations.
-    acc = xq @ w.T exactly (int32, = torch._int_mm); y = float(acc) * float32(scale * s_x) (+ bias)."""
+    acc = xq @ w.T exactly (int32, = torch._int_mm); y = float(acc) * float32(scale * s_x) (+ bias),
+    then the fused act / residual of penta_linear."""
     assert xq.is_cuda and xq.dtype == torch.int8 and xq.dim() == 2
     assert packed_w.dtype == torch.int32
     M, pitch = xq.shape
     N, K_packs = packed_w.shape
     assert K_packs == _k_packs(K_orig), "packed weights do not match K_orig"
+    act_code, res = _epilogue_args(act, residual, (M,), N, xq.device)
+    assert out_dtype is not None or (act_code == _nat.PN_ACT_NONE and res is None), "epilogue ops need an output"
     pw, ld = _packed_rows(packed_w)
     y = torch.empty(M, N, device=xq.device, dtype=out_dtype) if out_dtype is not None else None
     acc = torch.empty(M, N, device=xq.device, dtype=torch.int32) if return_acc else None
@@ -261,22 +291,28 @@ def penta_linear_i8_prequant(xq: torch.Tensor, s_x: torch.Tensor, rowsum: torch.
     ws_bytes = int(L.pn_linear_workspace_size(_nat.PN_I8, M, N, K_orig))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=xq.device) if ws_bytes else None
     ydt = _nat.PN_F32 if out_dtype == torch.float32 else _nat.PN_BF16
-    _nat.check(L.pn_linear_i8_ld(xq.data_ptr(), pitch, s_x.data_ptr(), rowsum.data_ptr(), M, K_orig,
-                                 pw.data_ptr(), N, K_packs, ld, ctypes.c_float(scale), _nat.ptr(b), _nat.ptr(y), ydt,
-                                 _nat.ptr(acc), _nat.ptr(ws), ws_bytes, _nat.stream_of(xq)), "penta_linear_i8")
+    _nat.check(L.pn_linear_i8_epi(xq.data_ptr(), pitch, s_x.data_ptr(), rowsum.data_ptr(), M, K_orig,
+                                  pw.data_ptr(), N, K_packs, ld, ctypes.c_float(scale), _nat.ptr(b), act_code,
+                                  _nat.ptr(res), N, _nat.ptr(y), ydt, _nat.ptr(acc), _nat.ptr(ws), ws_bytes,
+                                  _nat.stream_of(xq)), "penta_linear_i8")
     return (y, acc) if return_acc else y
 
 
 def penta_linear_i8(x: torch.Tensor, packed_w: torch.Tensor, scale: float, K_orig: int,
                     bias: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
-                    return_acc: bool = False):
+                    return_acc: bool = False, act: str | None = None, residual: torch.Tensor | None = None):
     """Prefill path: per-token int8 activations x packed weights on the int8
-    tensor cores, fused scale epilogue.  x: (..., K) bf16/fp32 CUDA."""
+    tensor cores, fused scale epilogue (+ bias, act, residual as penta_linear).
+    x: (..., K) bf16/fp32 CUDA."""
     orig_shape = x.shape
     assert orig_shape[-1] == K_orig, f"Activation K={orig_shape[-1]} must match K_orig={K_orig}"
-    xq, s_x, rowsum = quantize_activations_i8(x)
-    out = penta_linear_i8_prequant(xq, s_x, rowsum, K_orig, packed_w, scale, bias, out_dtype, return_acc)
     N = packed_w.shape[0]
+    if residual is not None:
+        assert tuple(residual.shape) == (*orig_shape[:-1], N), "residual must match the output shape"
+        residual = residual.reshape(-1, N)
+    xq, s_x, rowsum = quantize_activations_i8(x)
+    out = penta_linear_i8_prequant(xq, s_x, rowsum, K_orig, packed_w, scale, bias, out_dtype, return_acc,
+                                   act=act, residual=residual)
     if return_acc:
         y, acc = out
         return y.reshape(*orig_shape[:-1], N), acc.reshape(*orig_shape[:-1], N)

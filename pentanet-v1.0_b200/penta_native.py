@@ -19,13 +19,15 @@ LIB_NAME = "libpentanet_b200.so"
 PN_OK, PN_ERR_ARG, PN_ERR_SHAPE, PN_ERR_ALIGN, PN_ERR_DTYPE = 0, 1, 2, 3, 4
 PN_ERR_CUDA, PN_ERR_UNSUPPORTED, PN_ERR_TIMEOUT, PN_ERR_WORKSPACE = 5, 6, 7, 8
 PN_F32, PN_BF16, PN_I8, PN_I32 = 0, 1, 2, 3
+PN_ACT_NONE, PN_ACT_GELU = 0, 1
 
 # Functions the header declares; tests check the library exports each one.
 EXPORTS = (
     "pn_abi_version", "pn_status_string", "pn_last_error", "pn_device_status", "pn_device_sm_count",
     "pn_absmean_workspace_size", "pn_absmean_scale", "pn_quantize_pack", "pn_quantize_pack_ternary", "pn_unpack",
     "pn_linear_workspace_size", "pn_linear_workspace_min_size", "pn_linear_bf16", "pn_linear_bf16_ld", "pn_packed_ld",
-    "pn_linear_bf16_nows", "pn_act_i8_pitch", "pn_quant_act_i8", "pn_linear_i8", "pn_linear_i8_ld",
+    "pn_linear_bf16_nows", "pn_linear_bf16_epi", "pn_act_i8_pitch", "pn_quant_act_i8", "pn_linear_i8",
+    "pn_linear_i8_ld", "pn_linear_i8_epi",
     "pn_ipc_handle", "pn_ipc_open", "pn_ipc_close",
     "pn_linear_bf16_peers", "pn_peer_barrier",
 )
@@ -67,12 +69,14 @@ def load() -> ctypes.CDLL:
         "pn_linear_workspace_min_size": (SZ, [I, I64, I64, I64]),
         "pn_linear_bf16": (I, [P, I64, I64, P, I64, I64, F, P, P, I, P, SZ, P]),
         "pn_linear_bf16_ld": (I, [P, I64, I64, P, I64, I64, I64, F, P, P, I, P, SZ, P]),
+        "pn_linear_bf16_epi": (I, [P, I64, I64, P, I64, I64, I64, F, P, I, P, I64, P, I, P, SZ, P]),
         "pn_packed_ld": (I64, [I64]),
         "pn_linear_bf16_nows": (I, [P, I64, I64, P, I64, I64, F, P, P, I, P]),
         "pn_act_i8_pitch": (I64, [I64]),
         "pn_quant_act_i8": (I, [P, I, I64, I64, P, I64, P, P, P]),
         "pn_linear_i8": (I, [P, I64, P, P, I64, I64, P, I64, I64, F, P, P, I, P, P, SZ, P]),
         "pn_linear_i8_ld": (I, [P, I64, P, P, I64, I64, P, I64, I64, I64, F, P, P, I, P, P, SZ, P]),
+        "pn_linear_i8_epi": (I, [P, I64, P, P, I64, I64, P, I64, I64, I64, F, P, I, P, I64, P, I, P, P, SZ, P]),
         "pn_ipc_handle": (I, [P, P, ctypes.POINTER(SZ)]),
         "pn_ipc_open": (I, [P, ctypes.POINTER(P)]),
         "pn_ipc_close": (I, [P]),

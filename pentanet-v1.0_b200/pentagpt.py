@@ -4,10 +4,12 @@ A GPT-2-style decoder with the architecture of the reference's PentaGPT
 (train_pentagpt.py:46-136; GPTConfig size 'large': 12 layers, 12 heads,
 d_model 768, MLP 3072, no biases, weight-tied lm_head) in which every
 projection -- c_attn, attention c_proj, c_fc, MLP c_proj and the lm_head -- is
-a PentaLinearFast (3-bit packed weights, fused dequant-matmul).  LayerNorm,
-GELU, residual adds and causal attention stay dense bf16 (attention through
-torch's scaled_dot_product_attention, the memory-efficient equivalent of the
-reference's masked softmax).
+a PentaLinearFast (3-bit packed weights, fused dequant-matmul).  The MLP's
+GELU and both residual adds run in the epilogues of the projections that
+produce their inputs (c_fc, attention c_proj, MLP c_proj), rounded as the
+separate bf16 ops round them; LayerNorm and causal attention stay dense bf16
+(attention through torch's scaled_dot_product_attention, the memory-efficient
+equivalent of the reference's masked softmax).
 
 `PentaGPTFast.random(seed)` builds the model from random weights, as used for
 throughput measurement; a trained reference model converts with
@@ -66,9 +68,8 @@ class _Block(nn.Module):
         v = v.view(B, T, self.n_head, C // self.n_head).transpose(1, 2)
         y = F.scaled_dot_product_attention(q, k, v, is_causal=True)
         y = y.transpose(1, 2).contiguous().view(B, T, C)
-        x = x + self.attn_proj(y)
-        h = self.mlp_proj(F.gelu(self.c_fc(self.ln_2(x))))
-        return x + h
+        x = self.attn_proj(y, residual=x)  # x + attn(ln_1(x)), train_pentagpt.py:100
+        return self.mlp_proj(self.c_fc(self.ln_2(x), act="gelu"), residual=x)  # x + mlp(ln_2(x)), :101
 
 
 class PentaGPTFast(nn.Module):

@@ -118,12 +118,15 @@ class PentaLinearFast(nn.Module):
         if prefix + 'k_orig_buf' in state_dict:
             self.K_orig = int(state_dict[prefix + 'k_orig_buf'])
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, act: str | None = None, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """y = x @ W.T * scale (+ bias); optionally act='gelu' and a bf16
+        `residual` added last, both fused into the product's epilogue."""
         if self.act_quant == 'int8':
-            return _pk.penta_linear_i8(x, self.packed_w, self.scale, self.K_orig, self.bias)
+            return _pk.penta_linear_i8(x, self.packed_w, self.scale, self.K_orig, self.bias, act=act,
+                                       residual=residual)
         if x.dtype != torch.bfloat16:
             x = x.to(torch.bfloat16)
-        return _penta_linear_fast(x, self.packed_w, self.scale, self.K_orig, self.bias)
+        return _penta_linear_fast(x, self.packed_w, self.scale, self.K_orig, self.bias, act=act, residual=residual)
 
     def extra_repr(self) -> str:
         N, K_packs = self.packed_w.shape
