@@ -355,6 +355,20 @@ def pentagpt_forward(dev):
     return res
 
 
+def run_profile_gpt(args):
+    """PentaGPT-124M bf16 forward (batch 32 x 1024), three calls, for a launch
+    list of one forward under ncu (skip the first two calls' launches)."""
+    import torch
+    from pentagpt import PentaGPTFast
+    dev = torch.device("cuda", 0)
+    idx = torch.randint(0, 50257, (32, 1024), generator=torch.Generator().manual_seed(42)).to(dev)
+    model = PentaGPTFast.random(seed=42, device=dev)
+    for _ in range(3):
+        model(idx)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": "pentagpt_124m_fwd", "forwards": 3}))
+
+
 def run_profile_prefill(args):
     """Small case for ncu: the int8 prefill GEMM at M = 4096, K = N = 4096,
     three warm-up launches and one measured launch (activations quantised
@@ -611,9 +625,13 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the int8 prefill secondary measurement")
     ap.add_argument("--profile", action="store_true", help="small fixed case for ncu captures")
     ap.add_argument("--profile-prefill", action="store_true", help="int8 prefill case for ncu captures")
+    ap.add_argument("--profile-gpt", action="store_true", help="PentaGPT-124M forward for ncu launch lists")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.profile_gpt:
+        run_profile_gpt(args)
+        return
     if args.profile_prefill:
         run_profile_prefill(args)
         return

@@ -193,6 +193,16 @@ int pn_linear_i8_epi(const int8_t *xq, int64_t xq_pitch, const float *s_x, const
                      const void *bias, int act, const void *residual, int64_t ld_res, void *y, int y_dtype,
                      int32_t *acc_out, void *workspace, size_t workspace_bytes, void *stream);
 
+/* LayerNorm over the last dimension: y[m, :] = (x[m, :] - mean) *
+ * rsqrt(var + eps) * weight + bias with fp32 mean and biased variance of the
+ * row; x and y PN_BF16 or PN_F32 (row-major, C elements per row), weight and
+ * bias NULL or C fp32 values, y rounded once.  Replaces the three kernels
+ * torch runs for nn.LayerNorm under bf16 autocast in the reference GPT (fp32
+ * cast, layer_norm, bf16 cast of the output; train_pentagpt.py:94-96,113,
+ * 100-101,127).  In place (y == x) when the dtypes match. */
+int pn_layer_norm(const void *x, int x_dtype, int64_t M, int64_t C, const float *weight, const float *bias,
+                  float eps, void *y, int y_dtype, void *stream);
+
 /* Number of SMs of the current device (used to size launches and shards). */
 int pn_device_sm_count(int *count_out);
 

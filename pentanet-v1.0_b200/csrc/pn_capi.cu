@@ -262,6 +262,22 @@ int pn_linear_bf16_epi(const void* x, int64_t M, int64_t K, const int32_t* packe
                             workspace, workspace_bytes, stream, nullptr, 0, 0, 0, "pn_linear_bf16_epi");
 }
 
+int pn_layer_norm(const void* x, int x_dtype, int64_t M, int64_t C, const float* weight, const float* bias, float eps,
+                  void* y, int y_dtype, void* stream) {
+    if (M > 0 && (!x || !y)) return fail(PN_ERR_ARG, "pn_layer_norm: null pointer");
+    if ((x_dtype != PN_F32 && x_dtype != PN_BF16) || (y_dtype != PN_F32 && y_dtype != PN_BF16))
+        return fail(PN_ERR_DTYPE, "pn_layer_norm: x_dtype %d y_dtype %d", x_dtype, y_dtype);
+    if (M < 0 || C < 1 || C > 0x7fffffff || !(eps >= 0.0f))
+        return fail(PN_ERR_SHAPE, "pn_layer_norm: M=%lld C=%lld eps=%g", (long long)M, (long long)C, (double)eps);
+    if (!aligned(x, x_dtype == PN_F32 ? 4 : 2) || !aligned(y, y_dtype == PN_F32 ? 4 : 2) || !aligned(weight, 4) ||
+        !aligned(bias, 4))
+        return fail(PN_ERR_ALIGN, "pn_layer_norm: misaligned pointer");
+    if (x == y && x_dtype != y_dtype) return fail(PN_ERR_ARG, "pn_layer_norm: in place needs x_dtype == y_dtype");
+    if (int st = check_device()) return st;
+    cudaError_t e = pn::launch_layer_norm(x, x_dtype, M, C, weight, bias, eps, y, y_dtype, (cudaStream_t)stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "pn_layer_norm");
+}
+
 int64_t pn_act_i8_pitch(int64_t K) { return pn::act_i8_pitch(K); }
 
 int pn_quant_act_i8(const void* x, int x_dtype, int64_t M, int64_t K, int8_t* xq, int64_t xq_pitch, float* s_x,

@@ -16,6 +16,10 @@ int64_t act_i8_pitch(int64_t K);
 cudaError_t launch_quant_act_i8(const void* x, int x_dtype, int64_t M, int64_t K, int8_t* xq, int64_t pitch,
                                 float* s_x, int32_t* rowsum, cudaStream_t s);
 
+// LayerNorm over the last dimension (C) of M rows; w, b: NULL or C fp32 values.
+cudaError_t launch_layer_norm(const void* x, int x_dtype, int64_t M, int64_t C, const float* w, const float* b,
+                              float eps, void* y, int y_dtype, cudaStream_t s);
+
 // Fused dequant-matmul on the tensor cores (tcgen05, A operand in TMEM).
 struct LinearArgs {
     int kind;                 // PN_BF16 (kind::f16) or PN_I8 (kind::i8)

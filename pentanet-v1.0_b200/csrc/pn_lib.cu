@@ -7,6 +7,7 @@
 
 #include "pn_pack.cu"
 #include "pn_act.cu"
+#include "pn_norm.cu"
 #include "pn_dqmm.cu"
 #include "pn_simt.cu"
 #include "pn_capi.cu"

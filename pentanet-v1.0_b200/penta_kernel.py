@@ -247,6 +247,28 @@ def penta_linear(x: torch.Tensor, packed_w: torch.Tensor, scale: float, K_orig: 
     return y.reshape(*orig_shape[:-1], N)
 
 
+def layer_norm(x: torch.Tensor, weight: torch.Tensor | None = None, bias: torch.Tensor | None = None,
+               eps: float = 1e-5, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """LayerNorm over the last dimension in one pass, output in out_dtype: what
+    nn.LayerNorm under bf16 autocast followed by a cast to bf16 computes (fp32
+    statistics, biased variance; train_pentagpt.py:94-96,127), without the
+    fp32 round trip.  x: (..., C) bf16/fp32 CUDA; weight, bias: (C,) or None."""
+    assert x.is_cuda and x.dtype in (torch.bfloat16, torch.float32)
+    assert out_dtype in (torch.bfloat16, torch.float32)
+    C = x.shape[-1]
+    x2 = x.contiguous().reshape(-1, C)
+    wf = weight.detach().to(device=x.device, dtype=torch.float32).contiguous() if weight is not None else None
+    bf = bias.detach().to(device=x.device, dtype=torch.float32).contiguous() if bias is not None else None
+    assert wf is None or wf.numel() == C
+    assert bf is None or bf.numel() == C
+    y = torch.empty(x2.shape, dtype=out_dtype, device=x.device)
+    dt = lambda t: _nat.PN_F32 if t == torch.float32 else _nat.PN_BF16
+    L = _nat.load()
+    _nat.check(L.pn_layer_norm(x2.data_ptr(), dt(x2.dtype), x2.shape[0], C, _nat.ptr(wf), _nat.ptr(bf),
+                               ctypes.c_float(eps), y.data_ptr(), dt(out_dtype), _nat.stream_of(x2)), "layer_norm")
+    return y.reshape(x.shape)
+
+
 # ── int8 activation path ─────────────────────────────────────────────────────
 
 def quantize_activations_i8(x: torch.Tensor):

@@ -27,7 +27,7 @@ EXPORTS = (
     "pn_absmean_workspace_size", "pn_absmean_scale", "pn_quantize_pack", "pn_quantize_pack_ternary", "pn_unpack",
     "pn_linear_workspace_size", "pn_linear_workspace_min_size", "pn_linear_bf16", "pn_linear_bf16_ld", "pn_packed_ld",
     "pn_linear_bf16_nows", "pn_linear_bf16_epi", "pn_act_i8_pitch", "pn_quant_act_i8", "pn_linear_i8",
-    "pn_linear_i8_ld", "pn_linear_i8_epi",
+    "pn_linear_i8_ld", "pn_linear_i8_epi", "pn_layer_norm",
     "pn_ipc_handle", "pn_ipc_open", "pn_ipc_close",
     "pn_linear_bf16_peers", "pn_peer_barrier",
 )
@@ -77,6 +77,7 @@ def load() -> ctypes.CDLL:
         "pn_linear_i8": (I, [P, I64, P, P, I64, I64, P, I64, I64, F, P, P, I, P, P, SZ, P]),
         "pn_linear_i8_ld": (I, [P, I64, P, P, I64, I64, P, I64, I64, I64, F, P, P, I, P, P, SZ, P]),
         "pn_linear_i8_epi": (I, [P, I64, P, P, I64, I64, P, I64, I64, I64, F, P, I, P, I64, P, I, P, P, SZ, P]),
+        "pn_layer_norm": (I, [P, I, I64, I64, P, P, F, P, I, P]),
         "pn_ipc_handle": (I, [P, P, ctypes.POINTER(SZ)]),
         "pn_ipc_open": (I, [P, ctypes.POINTER(P)]),
         "pn_ipc_close": (I, [P]),

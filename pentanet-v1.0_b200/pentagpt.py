@@ -7,9 +7,11 @@ projection -- c_attn, attention c_proj, c_fc, MLP c_proj and the lm_head -- is
 a PentaLinearFast (3-bit packed weights, fused dequant-matmul).  The MLP's
 GELU and both residual adds run in the epilogues of the projections that
 produce their inputs (c_fc, attention c_proj, MLP c_proj), rounded as the
-separate bf16 ops round them; LayerNorm and causal attention stay dense bf16
-(attention through torch's scaled_dot_product_attention, the memory-efficient
-equivalent of the reference's masked softmax).
+separate bf16 ops round them.  Each LayerNorm is one pass from bf16 to bf16
+with fp32 statistics (penta_kernel.layer_norm: what nn.LayerNorm under bf16
+autocast plus the cast in front of the projection compute, without the fp32
+round trip).  Causal attention is torch's scaled_dot_product_attention, the
+memory-efficient equivalent of the reference's masked softmax.
 
 `PentaGPTFast.random(seed)` builds the model from random weights, as used for
 throughput measurement; a trained reference model converts with
@@ -61,7 +63,7 @@ class _Block(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         B, T, C = x.shape
-        h = self.ln_1(x)
+        h = pk.layer_norm(x, self.ln_1.weight, self.ln_1.bias, self.ln_1.eps)
         q, k, v = self.c_attn(h).split(C, dim=2)
         q = q.view(B, T, self.n_head, C // self.n_head).transpose(1, 2)
         k = k.view(B, T, self.n_head, C // self.n_head).transpose(1, 2)
@@ -69,7 +71,8 @@ class _Block(nn.Module):
         y = F.scaled_dot_product_attention(q, k, v, is_causal=True)
         y = y.transpose(1, 2).contiguous().view(B, T, C)
         x = self.attn_proj(y, residual=x)  # x + attn(ln_1(x)), train_pentagpt.py:100
-        return self.mlp_proj(self.c_fc(self.ln_2(x), act="gelu"), residual=x)  # x + mlp(ln_2(x)), :101
+        h = pk.layer_norm(x, self.ln_2.weight, self.ln_2.bias, self.ln_2.eps)
+        return self.mlp_proj(self.c_fc(h, act="gelu"), residual=x)  # x + mlp(ln_2(x)), :101
 
 
 class PentaGPTFast(nn.Module):
@@ -116,10 +119,9 @@ class PentaGPTFast(nn.Module):
         assert T <= self.cfg.block_size
         pos = torch.arange(T, device=idx.device)
         x = (self.wte(idx) + self.wpe(pos)).to(torch.bfloat16)
-        with torch.autocast("cuda", dtype=torch.bfloat16):
-            for block in self.h:
-                x = block(x)
-            x = self.ln_f(x)
+        for block in self.h:
+            x = block(x)
         if not all_logits:
-            x = x[:, [-1], :]
-        return self.lm_head(x.to(torch.bfloat16).contiguous())
+            x = x[:, [-1], :]  # LayerNorm is per position: normalise only what the lm_head reads
+        x = pk.layer_norm(x, self.ln_f.weight, self.ln_f.bias, self.ln_f.eps)
+        return self.lm_head(x)

@@ -123,6 +123,26 @@ def test_pentagpt_block_fused_matches_unfused(cuda_device):
         x1 = x + blk.attn_proj(yv)
         want = x1 + blk.mlp_proj(F.gelu(blk.c_fc(blk.ln_2(x1))))
     err = (got.float() - want.float()).abs()
-    # equal except where a GELU rounding differs by one ulp and propagates
-    assert (err > 0).float().mean().item() < 1e-2
+    # equal up to one-ulp rounding differences (GELU's erff, the one-pass
+    # LayerNorm's fp32 statistics) and what they change downstream
+    assert err.mean().item() <= 2e-3 * want.float().abs().mean().item()
     assert err.max().item() <= 0.05 * want.float().abs().max().item()
+
+
+@pytest.mark.parametrize("M,C", [(1, 768), (300, 768), (64, 1024), (33, 2048), (17, 100), (5, 3000), (4096, 256)])
+@pytest.mark.parametrize("x_dtype", [torch.bfloat16, torch.float32])
+def test_layer_norm(cuda_device, M, C, x_dtype):
+    """One-pass LayerNorm against torch's fp32 layer_norm of the same values
+    (what nn.LayerNorm computes under bf16 autocast), rounded to bf16 or kept
+    in fp32."""
+    import penta_kernel as pk
+    x = (gen_act(M, C, seed=M + C) * 3 + 0.5).to(x_dtype).to(cuda_device)
+    w = gen_weight(1, C, seed=C, std=0.3)[0].add(1.0).to(cuda_device)
+    b = gen_weight(1, C, seed=C + 1, std=0.1)[0].to(cuda_device)
+    for wt, bt in ((w, None), (w, b), (None, None)):
+        ref = F.layer_norm(x.float(), (C,), wt, bt, 1e-5)
+        got32 = pk.layer_norm(x, wt, bt, 1e-5, out_dtype=torch.float32)
+        assert torch.allclose(got32, ref, rtol=2e-5, atol=2e-5), (got32 - ref).abs().max().item()
+        got = pk.layer_norm(x, wt, bt, 1e-5)
+        assert got.dtype == torch.bfloat16 and got.shape == x.shape
+        _gelu_close(got, ref.to(torch.bfloat16), f"layer_norm C={C}")
