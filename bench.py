@@ -369,6 +369,25 @@ def run_profile_gpt(args):
     print(json.dumps({"profile": "pentagpt_124m_fwd", "forwards": 3}))
 
 
+def run_profile_epilogue(args):
+    """The PentaGPT c_fc product (M 32768, K 768 -> N 3072, bf16) without and
+    with the GELU fused into its epilogue, three times each, alternating (for
+    ncu: skip 4 dqmm launches, capture 2)."""
+    import torch
+    import penta_kernel as pk
+    dev = torch.device("cuda", 0)
+    M, N, K = 32768, 3072, 768
+    g = torch.Generator(device=dev).manual_seed(1)
+    packed, _, gamma = pk.quantize_and_pack(torch.randn(N, K, device=dev, generator=g) * 0.02)
+    packed = pk.pad_packed(packed)
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    for _ in range(3):
+        pk.penta_linear(x, packed, gamma, K)
+        pk.penta_linear(x, packed, gamma, K, act="gelu")
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": "c_fc plain / fused gelu", "M": M, "N": N, "K": K}))
+
+
 def run_profile_prefill(args):
     """Small case for ncu: the int8 prefill GEMM at M = 4096, K = N = 4096,
     three warm-up launches and one measured launch (activations quantised
@@ -626,11 +645,15 @@ def main():
     ap.add_argument("--profile", action="store_true", help="small fixed case for ncu captures")
     ap.add_argument("--profile-prefill", action="store_true", help="int8 prefill case for ncu captures")
     ap.add_argument("--profile-gpt", action="store_true", help="PentaGPT-124M forward for ncu launch lists")
+    ap.add_argument("--profile-epilogue", action="store_true", help="plain vs fused-GELU product for ncu")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.profile_gpt:
         run_profile_gpt(args)
+        return
+    if args.profile_epilogue:
+        run_profile_epilogue(args)
         return
     if args.profile_prefill:
         run_profile_prefill(args)

@@ -106,14 +106,15 @@ def test_epilogue_argument_errors(cuda_device):
     assert st == nat.PN_ERR_SHAPE
 
 
-def test_pentagpt_block_fused_matches_unfused(cuda_device):
-    """One PentaGPT block with the fused epilogues against the same block run
-    with separate torch ops."""
+@pytest.mark.parametrize("B,T", [(2, 32), (1, 7), (2, 256)])
+def test_pentagpt_block_fused_matches_unfused(cuda_device, B, T):
+    """One PentaGPT block (fused epilogues at decode-sized token counts,
+    separate ops above) against the same block run with separate torch ops."""
     from pentagpt import PentaGPTConfig, PentaGPTFast
     cfg = PentaGPTConfig(n_layer=1, n_head=12, n_embd=768, block_size=256, vocab_size=512)
     model = PentaGPTFast.random(cfg, seed=3, device=cuda_device)
     blk = model.h[0]
-    x = (gen_act(2 * 256, 768, seed=4) * 0.3).to(torch.bfloat16).to(cuda_device).view(2, 256, 768)
+    x = (gen_act(B * T, 768, seed=4) * 0.3).to(torch.bfloat16).to(cuda_device).view(B, T, 768)
     with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
         got = blk(x)
         B, T, C = x.shape
