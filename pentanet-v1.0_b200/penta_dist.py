@@ -383,7 +383,7 @@ def linear_peers(x: torch.Tensor, packed_local: torch.Tensor, scale: float, K_or
     assert K == K_orig
     N, KP = packed_local.shape
     L = nat.load()
-    ws_bytes = int(L.pn_linear_workspace_size(nat.PN_BF16, M, N, K))
+    ws_bytes = nat.linear_workspace_size(nat.PN_BF16, M, N, K, x.device)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
     arr = (ctypes.c_void_p * len(out_ptrs))(*out_ptrs)
     s = stream if stream is not None else torch.cuda.current_stream(x.device)

@@ -233,7 +233,7 @@ def penta_linear(x: torch.Tensor, packed_w: torch.Tensor, scale: float, K_orig: 
         b = bias.detach().to(device=x.device, dtype=torch.bfloat16).contiguous()
         assert b.numel() == N
     L = _nat.load()
-    ws_bytes = int(L.pn_linear_workspace_size(_nat.PN_BF16, M, N, K))
+    ws_bytes = _nat.linear_workspace_size(_nat.PN_BF16, M, N, K, x.device)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
     ydt = _nat.PN_F32 if out_dtype == torch.float32 else _nat.PN_BF16
     if act_code == _nat.PN_ACT_NONE and res is None:
@@ -310,7 +310,7 @@ def penta_linear_i8_prequant(xq: torch.Tensor, s_x: torch.Tensor, rowsum: torch.
     acc = torch.empty(M, N, device=xq.device, dtype=torch.int32) if return_acc else None
     b = bias.detach().to(device=xq.device, dtype=torch.bfloat16).contiguous() if bias is not None else None
     L = _nat.load()
-    ws_bytes = int(L.pn_linear_workspace_size(_nat.PN_I8, M, N, K_orig))
+    ws_bytes = _nat.linear_workspace_size(_nat.PN_I8, M, N, K_orig, xq.device)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=xq.device) if ws_bytes else None
     ydt = _nat.PN_F32 if out_dtype == torch.float32 else _nat.PN_BF16
     _nat.check(L.pn_linear_i8_epi(xq.data_ptr(), pitch, s_x.data_ptr(), rowsum.data_ptr(), M, K_orig,
