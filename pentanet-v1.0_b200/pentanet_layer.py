@@ -35,10 +35,17 @@ _KERNEL_AVAILABLE = True
 class PentaLinear(nn.Module):
     """Linear layer constrained to {-2,-1,0,+1,+2} x absmean scale, trained with
     the straight-through estimator (pentanet_layer.py:17-65).  Dense torch math:
-    this is the training layer and the dense numeric reference."""
+    this is the training layer and the dense numeric reference.
 
-    def __init__(self, in_features, out_features, bias=True):
+    mode='bitnet' (not in the reference's PentaLinear; the ternary rule of its
+    GPT script's QuantLinear, train_pentagpt.py:33-36) clamps to {-1, 0, +1}
+    instead; to_fast_inference then packs the ternary codes in the same
+    format."""
+
+    def __init__(self, in_features, out_features, bias=True, mode='pentanet'):
         super().__init__()
+        assert mode in ('pentanet', 'bitnet')
+        self.mode = mode
         self.in_features = in_features
         self.out_features = out_features
         self.weight = nn.Parameter(torch.randn(out_features, in_features) * (1.0 / in_features ** 0.5))
@@ -49,7 +56,8 @@ class PentaLinear(nn.Module):
 
     def forward(self, x):
         scale = self.weight.abs().mean().clamp(min=1e-8)
-        w_quant = torch.clamp(torch.round(self.weight / scale), -2, 2)
+        qmax = 2 if self.mode == 'pentanet' else 1
+        w_quant = torch.clamp(torch.round(self.weight / scale), -qmax, qmax)
         w_ste = (w_quant * scale - self.weight).detach() + self.weight
         return F.linear(x, w_ste, self.bias)
 
