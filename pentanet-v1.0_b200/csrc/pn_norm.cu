@@ -39,16 +39,40 @@ struct Vec8<float> {
     }
 };
 
+// Eight consecutive row elements kept in their storage type (4 registers
+// for bf16), converted to fp32 on each use.
+template <typename T>
+struct RowVec8;
+template <>
+struct RowVec8<__nv_bfloat16> {
+    uint32_t w[4];
+    __device__ __forceinline__ void load(const __nv_bfloat16* p) {
+        const uint4 u = *reinterpret_cast<const uint4*>(p);
+        w[0] = u.x, w[1] = u.y, w[2] = u.z, w[3] = u.w;
+    }
+    __device__ __forceinline__ float get(int j) const {
+        return __uint_as_float((j & 1) ? (w[j >> 1] & 0xFFFF0000u) : (w[j >> 1] << 16));
+    }
+};
+template <>
+struct RowVec8<float> {
+    float f[8];
+    __device__ __forceinline__ void load(const float* p) { Vec8<float>::load(p, f); }
+    __device__ __forceinline__ float get(int j) const { return f[j]; }
+};
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
 }
 
-// Rows of C <= 256 * V elements (C % 8 == 0, 16-byte aligned rows), held in
-// registers: lane l owns the 8-element vectors l, l + 32, ...
+// Rows of C <= 256 * V elements (C % 8 == 0, 16-byte aligned rows, weight
+// and bias 16-byte aligned), held in registers: lane l owns the 8-element
+// vectors l, l + 32, ...  Five blocks per SM: the register cap keeps 40 warps
+// resident so enough loads are in flight.
 template <typename T, int V>
-__global__ void __launch_bounds__(kNormWarps * 32) layer_norm_reg_kernel(const T* __restrict__ x, int64_t M, int C,
+__global__ void __launch_bounds__(kNormWarps * 32, 5) layer_norm_reg_kernel(const T* __restrict__ x, int64_t M, int C,
                                                                          const float* __restrict__ w,
                                                                          const float* __restrict__ b, float eps,
                                                                          void* __restrict__ y, int y_f32) {
@@ -56,15 +80,15 @@ __global__ void __launch_bounds__(kNormWarps * 32) layer_norm_reg_kernel(const T
     const int64_t row = (int64_t)blockIdx.x * kNormWarps + (threadIdx.x >> 5);
     if (row >= M) return;
     const T* xr = x + row * C;
-    float v[V][8];
+    RowVec8<T> v[V];
     float s = 0.0f;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
         const int c = (i * 32 + lane) * 8;
         if (c < C) {
-            Vec8<T>::load(xr + c, v[i]);
+            v[i].load(xr + c);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) s += v[i][j];
+            for (int j = 0; j < 8; ++j) s += v[i].get(j);
         }
     }
     const float mean = __fdiv_rn(warp_sum(s), (float)C);
@@ -74,7 +98,7 @@ __global__ void __launch_bounds__(kNormWarps * 32) layer_norm_reg_kernel(const T
         if ((i * 32 + lane) * 8 < C) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                const float d = v[i][j] - mean;
+                const float d = v[i].get(j) - mean;
                 q = fmaf(d, d, q);
             }
         }
@@ -86,11 +110,18 @@ __global__ void __launch_bounds__(kNormWarps * 32) layer_norm_reg_kernel(const T
         if (c >= C) continue;
         float o[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            float t = (v[i][j] - mean) * rstd;
-            if (w) t *= __ldg(w + c + j);
-            if (b) t += __ldg(b + c + j);
-            o[j] = t;
+        for (int j = 0; j < 8; ++j) o[j] = (v[i].get(j) - mean) * rstd;
+        if (w) {
+            float wv[8];
+            Vec8<float>::load(w + c, wv);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] *= wv[j];
+        }
+        if (b) {
+            float bv[8];
+            Vec8<float>::load(b + c, bv);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] += bv[j];
         }
         if (y_f32) {
             float* yr = static_cast<float*>(y) + row * C + c;
@@ -153,17 +184,21 @@ template <typename T>
 static cudaError_t launch_norm_t(const T* x, int64_t M, int64_t C, const float* w, const float* b, float eps, void* y,
                                  int y_f32, cudaStream_t s) {
     const unsigned blocks = (unsigned)((M + kNormWarps - 1) / kNormWarps);
-    const bool vec = C % 8 == 0 && (reinterpret_cast<uintptr_t>(x) % 16) == 0 &&
-                     (reinterpret_cast<uintptr_t>(y) % 16) == 0;
+    auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) % 16) == 0; };
+    const bool vec = C % 8 == 0 && a16(x) && a16(y) && a16(w) && a16(b);
     const int c = (int)C;
+    // Register-held rows up to the width that compiles without spills at five
+    // blocks per SM: 1024 bf16 / 512 fp32 elements; wider rows take the
+    // strided kernel.
+    constexpr int kMaxC = sizeof(T) == 2 ? 1024 : 512;
     if (vec && C <= 256)
         layer_norm_reg_kernel<T, 1><<<blocks, kNormWarps * 32, 0, s>>>(x, M, c, w, b, eps, y, y_f32);
     else if (vec && C <= 512)
         layer_norm_reg_kernel<T, 2><<<blocks, kNormWarps * 32, 0, s>>>(x, M, c, w, b, eps, y, y_f32);
-    else if (vec && C <= 1024)
-        layer_norm_reg_kernel<T, 4><<<blocks, kNormWarps * 32, 0, s>>>(x, M, c, w, b, eps, y, y_f32);
-    else if (vec && C <= 2048)
-        layer_norm_reg_kernel<T, 8><<<blocks, kNormWarps * 32, 0, s>>>(x, M, c, w, b, eps, y, y_f32);
+    else if (vec && C <= 768 && C <= kMaxC)
+        layer_norm_reg_kernel<T, sizeof(T) == 2 ? 3 : 2><<<blocks, kNormWarps * 32, 0, s>>>(x, M, c, w, b, eps, y, y_f32);
+    else if (vec && C <= kMaxC)
+        layer_norm_reg_kernel<T, sizeof(T) == 2 ? 4 : 2><<<blocks, kNormWarps * 32, 0, s>>>(x, M, c, w, b, eps, y, y_f32);
     else
         layer_norm_any_kernel<T><<<blocks, kNormWarps * 32, 0, s>>>(x, M, C, w, b, eps, y, y_f32);
     return cudaGetLastError();

@@ -130,7 +130,8 @@ def test_pentagpt_block_fused_matches_unfused(cuda_device, B, T):
     assert err.max().item() <= 0.05 * want.float().abs().max().item()
 
 
-@pytest.mark.parametrize("M,C", [(1, 768), (300, 768), (64, 1024), (33, 2048), (17, 100), (5, 3000), (4096, 256)])
+@pytest.mark.parametrize("M,C", [(1, 768), (300, 768), (64, 1024), (33, 2048), (17, 100), (5, 3000), (4096, 256),
+                                 (9, 512), (70, 640)])
 @pytest.mark.parametrize("x_dtype", [torch.bfloat16, torch.float32])
 def test_layer_norm(cuda_device, M, C, x_dtype):
     """One-pass LayerNorm against torch's fp32 layer_norm of the same values
@@ -147,3 +148,14 @@ def test_layer_norm(cuda_device, M, C, x_dtype):
         got = pk.layer_norm(x, wt, bt, 1e-5)
         assert got.dtype == torch.bfloat16 and got.shape == x.shape
         _gelu_close(got, ref.to(torch.bfloat16), f"layer_norm C={C}")
+
+
+def test_layer_norm_unaligned_weight(cuda_device):
+    """A weight view that is not 16-byte aligned takes the strided kernel."""
+    import penta_kernel as pk
+    x = gen_act(40, 768, seed=2).to(torch.bfloat16).to(cuda_device)
+    w = (gen_weight(1, 769, seed=3, std=0.3)[0] + 1.0).to(cuda_device)[1:]
+    assert w.data_ptr() % 16 != 0
+    ref = F.layer_norm(x.float(), (768,), w, None, 1e-5)
+    got32 = pk.layer_norm(x, w, None, 1e-5, out_dtype=torch.float32)
+    assert torch.allclose(got32, ref, rtol=2e-5, atol=2e-5)
