@@ -324,6 +324,69 @@ def prefill_int8(dev, gen, peaks):
             "per_shape": rows}
 
 
+def pack_secondary(dev, peaks):
+    """Secondary measurement: quantise + 3-bit pack of the 70B-class fp32
+    master weights on the device (pn_absmean_scale, then pn_quantize_pack,
+    gamma kept on the device), and the pack kernel alone with gamma given.
+    Algorithmic bytes: one read of W (4 N K) + the packed words (4 N K_packs);
+    the two-pass form reads W twice."""
+    import torch
+    import penta_kernel as pk
+    import penta_native as nat
+    L = nat.load()
+    res = {"workload": "quantize_and_pack of fp32 W 28672x8192 and 8192x28672 (940 MB each)", "unit": "GB/s"}
+    per = []
+    tot_b = tot_two = tot_one = 0.0
+    for (N, K) in ((28672, 8192), (8192, 28672)):
+        g = torch.Generator(device=dev).manual_seed(N)
+        w = torch.randn(N, K, device=dev, generator=g) * 0.02
+        kp = (K + 9) // 10
+        packed = torch.empty(N, kp, dtype=torch.int32, device=dev)
+        d_scale = torch.empty((), dtype=torch.float32, device=dev)
+        ws = torch.empty(int(L.pn_absmean_workspace_size()), dtype=torch.uint8, device=dev)
+        sp = torch.cuda.current_stream(dev).cuda_stream
+
+        def absmean():
+            nat.check(L.pn_absmean_scale(w.data_ptr(), nat.PN_F32, N * K, d_scale.data_ptr(), ws.data_ptr(),
+                                         ws.numel(), sp), "pn_absmean_scale")
+
+        def pack():
+            nat.check(L.pn_quantize_pack(w.data_ptr(), nat.PN_F32, N, K, d_scale.data_ptr(), packed.data_ptr(), sp),
+                      "pn_quantize_pack")
+
+        def timed(fn, reps=5):
+            fn()
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / reps * 1e-3
+
+        t_two = timed(lambda: (absmean(), pack()))
+        t_one = timed(pack)
+        b = 4.0 * N * K + 4.0 * N * kp
+        want, _, _ = pk.quantize_and_pack(w)
+        assert torch.equal(packed, want), "device-scale pack differs from quantize_and_pack"
+        per.append({"N": N, "K": K, "us_scale_and_pack": round(t_two * 1e6, 1), "us_pack": round(t_one * 1e6, 1)})
+        tot_b += b
+        tot_two += t_two
+        tot_one += t_one
+        del w, packed
+        torch.cuda.empty_cache()
+    res["value"] = round(tot_b / tot_two / 1e9, 1)
+    res["pack_only"] = round(tot_b / tot_one / 1e9, 1)
+    res["roofline"] = {"bound": "hbm", "achieved": res["value"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                       "frac": round(res["value"] / peaks["hbm_gbs"], 4),
+                       "frac_pack_only": round(res["pack_only"] / peaks["hbm_gbs"], 4),
+                       "kernel": "pn::absmean_partial/final + pn::quantize_pack_kernel<float>"}
+    res["per_shape"] = per
+    return res
+
+
 def pentagpt_forward(dev):
     """Secondary measurement: PentaGPT-124M forward (prefill) tokens/s -- 12
     layers, d 768, every projection packed, batch 32 x 1024 random token ids,
@@ -667,9 +730,11 @@ def run_ours(args):
 
     prefill = None
     gpt = None
+    packsec = None
     if world == 1 and not args.no_prefill:
         prefill = prefill_int8(dev, gen, peaks)
         gpt = pentagpt_forward(dev)
+        packsec = pack_secondary(dev, peaks)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -706,7 +771,7 @@ def run_ours(args):
             # per product: the activation re-layout kernel and the dqmm kernel
             # (+ the cross-GPU barrier kernel when sharded)
             "gpu_launches": (2 if world == 1 else 3) * len(seq) * args.steps,
-            "secondary": {"prefill_int8": prefill, "pentagpt_124m_fwd": gpt},
+            "secondary": {"prefill_int8": prefill, "pentagpt_124m_fwd": gpt, "quantize_pack": packsec},
             "clocks": sampler.summary() if sampler else None,
         }
         print(json.dumps(line), flush=True)

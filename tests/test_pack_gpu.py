@@ -101,3 +101,27 @@ def test_cfg4_size_pack_property(cuda_device):
     rows = [0, 1, 12345, 28671]
     want, _, _ = orc.quantize_pack(w[rows].cpu().numpy(), gamma)
     assert np.array_equal(packed[rows].cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("gamma", [0.0137, 0.3, 1e-8, 7.77, 0.015953034162521362])
+@pytest.mark.parametrize("mode", ["pentanet", "bitnet"])
+def test_pack_near_half_integer_quotients(cuda_device, gamma, mode):
+    """Weights within a few ulps of gamma * (k + 1/2) for every half-integer the
+    clamp can see: the codes must equal those of the IEEE quotient (the oracle
+    divides exactly like torch's weight / scale), whichever side of the tie
+    each value falls on."""
+    g32 = np.float32(gamma)
+    vals = []
+    for h in (-3.5, -2.5, -1.5, -0.5, 0.5, 1.5, 2.5, 3.5):
+        c = np.float32(h) * g32
+        for d in range(-4, 5):
+            v = c
+            step = np.float32(np.inf) if d > 0 else np.float32(-np.inf)
+            for _ in range(abs(d)):
+                v = np.nextafter(v, step, dtype=np.float32)
+            vals.append(v)
+    w = np.array(vals, dtype=np.float32).reshape(1, -1)
+    w = np.concatenate([w, -w[:, ::-1]], axis=0)
+    want, _, _ = orc.quantize_pack(w, float(g32), mode=mode)
+    got, K, _ = pk.quantize_and_pack(torch.from_numpy(w).to(cuda_device), scale=float(g32), mode=mode)
+    assert np.array_equal(got.cpu().numpy(), want)
