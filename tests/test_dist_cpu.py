@@ -225,3 +225,41 @@ def test_sharded_checkpoint_gloo_world2(tmp_path):
         d = np.load(tmp_path / f"s{r}.npz")
         assert d["refused"].all()
         assert float(d["scale"]) == float(np.float32(d["g"])) and bool(d["bias_ok"])
+
+
+def _empty_slice_worker(rank, world, port, out_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        N, K, M = 24, 80, 3
+        w = gen_weight(N, K, seed=51).numpy()
+        g = float(orc.absmean_scale(w))
+        p = orc.quantize_pack(w, g)[0]
+        dn = pd.RowShardedPentaLinear.from_full(torch.from_numpy(p), g, K, unit=40)
+        if dn.K_local > 0:  # an empty slice keeps the layer's own zero partial
+            dn.forward_local = lambda xl: torch.from_numpy(
+                orc.matmul_f64(xl.float().numpy(), orc.unpack(dn.packed_w.numpy(), dn.K_local), g).astype(np.float32))
+        x = gen_act(M, K, seed=52).float()
+        y = dn(x).float().numpy()
+        want = orc.bf16_linear_out(orc.matmul_f64(x.numpy(), orc.unpack(p, K), g).astype(np.float32))
+        np.savez(os.path.join(out_dir, f"e{rank}.npz"), y=y, want=want, k_local=dn.K_local,
+                 words=dn.packed_w.shape[1])
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_parallel_empty_slice_gloo_world3(tmp_path):
+    """A world larger than K's 40-column units leaves a rank without columns:
+    it holds no words, contributes a zero partial, and every rank still gets
+    the full product."""
+    from _util import assert_bf16_close
+    world = 3
+    mp.start_processes(_empty_slice_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn")
+    ks = []
+    for r in range(world):
+        d = np.load(tmp_path / f"e{r}.npz")
+        ks.append((int(d["k_local"]), int(d["words"])))
+        assert_bf16_close(d["y"], d["want"].astype(np.float64), f"rank {r}")
+    assert ks == [(40, 4), (40, 4), (0, 0)]
