@@ -84,7 +84,12 @@ __global__ void __launch_bounds__(kActThreads) quant_act_i8_kernel(const T* __re
 // 1.5 * 2^23 addition (round to nearest, ties to even, for |q| < 2^22; the
 // integer is then the low bits of the sum), all in FMA-pipe arithmetic.  The
 // rare elements near a half-integer, and NaN, take the exact division.
-constexpr int kActVecPieces = 16;  // 16-byte pieces per thread
+// 16-byte pieces per thread: 8 (64 bf16) for rows up to 256 * 64 elements,
+// 16 for rows up to twice that.  Sixteen pieces hold 64 registers of data
+// (80+ per thread, two blocks per SM), which made the 4096 x 4096 case
+// 1.5x slower than eight pieces with the same output.
+constexpr int kActVecPiecesSmall = 8;
+constexpr int kActVecPiecesLarge = 16;
 constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
 
 __device__ __forceinline__ int quant1(float xv, float s, float rs) {
@@ -97,7 +102,7 @@ __device__ __forceinline__ int quant1(float xv, float s, float rs) {
     return (int)r;
 }
 
-template <int TPT>
+template <int TPT, int kActVecPieces>
 __global__ void __launch_bounds__(kActThreads) quant_act_i8_vec_kernel(const uint4* __restrict__ x, int64_t M,
                                                                        int64_t K, int8_t* __restrict__ xq,
                                                                        int64_t pitch, float* __restrict__ s_x,
@@ -181,24 +186,34 @@ cudaError_t launch_quant_act_i8(const void* x, int x_dtype, int64_t M, int64_t K
     if (M == 0) return cudaSuccess;
     const bool vec = x_dtype == PN_BF16 && K % 8 == 0 && pitch % 8 == 0 &&
                      reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(xq) % 8 == 0;
-    // threads per token: the fewest covering the row's output pieces (16
-    // each), doubled while the grid would have fewer than ~2 blocks per SM
+    // pieces per thread: the fewer that lets kActThreads threads cover the row
+    const int pieces_pt = pitch <= (int64_t)kActThreads * 8 * kActVecPiecesSmall ? kActVecPiecesSmall
+                                                                                 : kActVecPiecesLarge;
+    // threads per token: the fewest covering the row's output pieces, doubled
+    // while the grid would have fewer than ~2 blocks per SM
     int tpt = 8;
-    while (tpt < kActThreads && (int64_t)tpt * 8 * kActVecPieces < pitch) tpt *= 2;
+    while (tpt < kActThreads && (int64_t)tpt * 8 * pieces_pt < pitch) tpt *= 2;
     const int64_t min_blocks = 2 * (int64_t)(device_sm_count() > 0 ? device_sm_count() : 148);
     while (tpt < kActThreads && M * tpt / kActThreads < min_blocks) tpt *= 2;
-    if (vec && (int64_t)tpt * 8 * kActVecPieces >= pitch) {
+    if (vec && (int64_t)tpt * 8 * pieces_pt >= pitch) {
         const int tokens = kActThreads / tpt;
         const unsigned blocks = (unsigned)((M + tokens - 1) / tokens);
         const uint4* xv = static_cast<const uint4*>(x);
-        switch (tpt) {
-            case 8: quant_act_i8_vec_kernel<8><<<blocks, kActThreads, 0, s>>>(xv, M, K, xq, pitch, s_x, rowsum); break;
-            case 16: quant_act_i8_vec_kernel<16><<<blocks, kActThreads, 0, s>>>(xv, M, K, xq, pitch, s_x, rowsum); break;
-            case 32: quant_act_i8_vec_kernel<32><<<blocks, kActThreads, 0, s>>>(xv, M, K, xq, pitch, s_x, rowsum); break;
-            case 64: quant_act_i8_vec_kernel<64><<<blocks, kActThreads, 0, s>>>(xv, M, K, xq, pitch, s_x, rowsum); break;
-            case 128: quant_act_i8_vec_kernel<128><<<blocks, kActThreads, 0, s>>>(xv, M, K, xq, pitch, s_x, rowsum); break;
-            default: quant_act_i8_vec_kernel<256><<<blocks, kActThreads, 0, s>>>(xv, M, K, xq, pitch, s_x, rowsum); break;
-        }
+        auto go = [&](auto pc) {
+            constexpr int PC = decltype(pc)::value;
+            switch (tpt) {
+                case 8: quant_act_i8_vec_kernel<8, PC><<<blocks, kActThreads, 0, s>>>(xv, M, K, xq, pitch, s_x, rowsum); break;
+                case 16: quant_act_i8_vec_kernel<16, PC><<<blocks, kActThreads, 0, s>>>(xv, M, K, xq, pitch, s_x, rowsum); break;
+                case 32: quant_act_i8_vec_kernel<32, PC><<<blocks, kActThreads, 0, s>>>(xv, M, K, xq, pitch, s_x, rowsum); break;
+                case 64: quant_act_i8_vec_kernel<64, PC><<<blocks, kActThreads, 0, s>>>(xv, M, K, xq, pitch, s_x, rowsum); break;
+                case 128: quant_act_i8_vec_kernel<128, PC><<<blocks, kActThreads, 0, s>>>(xv, M, K, xq, pitch, s_x, rowsum); break;
+                default: quant_act_i8_vec_kernel<256, PC><<<blocks, kActThreads, 0, s>>>(xv, M, K, xq, pitch, s_x, rowsum); break;
+            }
+        };
+        if (pieces_pt == kActVecPiecesSmall)
+            go(std::integral_constant<int, kActVecPiecesSmall>{});
+        else
+            go(std::integral_constant<int, kActVecPiecesLarge>{});
     } else if (x_dtype == PN_F32)
         quant_act_i8_kernel<float><<<(unsigned)M, kActThreads, 0, s>>>(static_cast<const float*>(x), K, xq, pitch,
                                                                         s_x, rowsum);
