@@ -145,17 +145,22 @@ int pn_linear_bf16_epi(const void *x, int64_t M, int64_t K, const int32_t *packe
  * place: K_packs rounded up to a multiple of 4. */
 int64_t pn_packed_ld(int64_t K_packs);
 
-/* pn_linear_bf16 without a workspace argument, for callers that cannot
+/* pn_linear_bf16_ld without a workspace argument, for callers that cannot
  * allocate device memory (code where no allocator may run, or embeddings that
  * hand the library only raw input/output pointers).  No counterpart in the
  * reference (its wrapper allocates with torch.empty, penta_kernel.py:259).
  * Scratch comes from one static 4 MiB device array per GPU (held until the
- * process exits); shapes needing more return PN_ERR_WORKSPACE.  Calls that
- * overlap on the GPU share that array and race: serialise them.  The first
- * call on a device looks up the array's address; make it before any stream
- * capture.  Allocates and frees nothing. */
+ * process exits).  A call needs the decode activation slab for M <= 64
+ * (3.7 MB at K = 28672 and 64 tokens) plus, when packed_ld % 4 != 0, a
+ * 16-byte-pitch copy of the weights (N * pn_packed_ld(K_packs) * 4 bytes,
+ * beyond the array for most layers): store the rows at pn_packed_ld(K_packs).
+ * Shapes needing more return PN_ERR_WORKSPACE before anything is enqueued.
+ * Calls that overlap on the GPU share the array and race: serialise them.
+ * The first call on a device looks up the array's address; make it before
+ * any stream capture, and do not use this entry point across a
+ * cudaDeviceReset.  Allocates and frees nothing. */
 int pn_linear_bf16_nows(const void *x, int64_t M, int64_t K, const int32_t *packed, int64_t N, int64_t K_packs,
-                        float scale, const void *bias, void *y, int y_dtype, void *stream);
+                        int64_t packed_ld, float scale, const void *bias, void *y, int y_dtype, void *stream);
 
 /* ---- int8 activation path: replaces the int8 line of the reference
  *      benchmark (penta_avx2_wrapper.py:130-131,137,147), per token --------- */

@@ -165,11 +165,11 @@ int pn_unpack(const int32_t* packed, int64_t N, int64_t K_packs, int64_t K_orig,
 }
 
 size_t pn_linear_workspace_size(int kind, int64_t M, int64_t N, int64_t K) {
-    return pn::linear_workspace_bytes(kind, M, N, K);
+    return pn::linear_workspace_bytes(kind, M, N, K, k_packs(K));
 }
 
 size_t pn_linear_workspace_min_size(int kind, int64_t M, int64_t N, int64_t K) {
-    return pn::linear_workspace_min_bytes(kind, M, N, K);
+    return pn::linear_workspace_min_bytes(kind, M, N, K, k_packs(K));
 }
 
 }  // extern "C"
@@ -193,10 +193,10 @@ int linear_bf16_impl(const void* x, int64_t M, int64_t K, const int32_t* packed,
     if (!aligned(x, 2) || !aligned(packed, 16) || !aligned(y, y_dtype == PN_F32 ? 4 : 2) || !aligned(bias, 2))
         return fail(PN_ERR_ALIGN, "%s: misaligned pointer (packed weights need 16-byte alignment)", name);
     if (int st = check_epilogue(residual, ld_res, act, N, y, n_peers, name)) return st;
-    const size_t need = pn::linear_workspace_min_bytes(PN_BF16, M, N, K);
+    const size_t need = pn::linear_workspace_min_bytes(PN_BF16, M, N, K, packed_ld);
     if (need > 0 && (!workspace || workspace_bytes < need))
         return fail(PN_ERR_WORKSPACE, "%s: workspace needs at least %zu bytes (%zu recommended)", name, need,
-                    pn::linear_workspace_bytes(PN_BF16, M, N, K));
+                    pn::linear_workspace_bytes(PN_BF16, M, N, K, packed_ld));
     if (int st = check_device()) return st;
     if (M == 0 || N == 0) return ok();
     pn::LinearArgs a{};
@@ -315,10 +315,10 @@ static int linear_i8_impl(const int8_t* xq, int64_t xq_pitch, const float* s_x, 
         return fail(PN_ERR_ALIGN, "pn_linear_i8: misaligned pointer");
     if ((residual || act != PN_ACT_NONE) && !y) return fail(PN_ERR_ARG, "pn_linear_i8: epilogue ops need y");
     if (int st = check_epilogue(residual, ld_res, act, N, y, 0, "pn_linear_i8")) return st;
-    const size_t need = pn::linear_workspace_min_bytes(PN_I8, M, N, K);
+    const size_t need = pn::linear_workspace_min_bytes(PN_I8, M, N, K, packed_ld);
     if (need > 0 && (!workspace || workspace_bytes < need))
         return fail(PN_ERR_WORKSPACE, "pn_linear_i8: workspace needs at least %zu bytes (%zu recommended)", need,
-                    pn::linear_workspace_bytes(PN_I8, M, N, K));
+                    pn::linear_workspace_bytes(PN_I8, M, N, K, packed_ld));
     if (int st = check_device()) return st;
     if (M == 0 || N == 0) return ok();
     pn::LinearArgs a{};

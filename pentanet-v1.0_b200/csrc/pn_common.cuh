@@ -304,6 +304,30 @@ constexpr uint32_t kDescHiSW32 = (256u >> 4) | (1u << 14) | (6u << 29);
 constexpr uint32_t kDescHiSW64 = (512u >> 4) | (1u << 14) | (4u << 29);
 constexpr uint32_t kDescHiSW128 = (1024u >> 4) | (1u << 14) | (2u << 29);
 
+// mma5_ts_warp (kind::f16) followed by a sixth MMA under the same election:
+// A at TMEM column a6, B at the 32-byte-swizzled slab whose descriptor low
+// word is lo6 (accumulating).
+__device__ __forceinline__ void mma5c_ts_warp(uint32_t d_tmem, uint32_t a_tmem, const uint32_t (&lo)[5],
+                                              const uint32_t (&hi)[5], uint32_t a6, uint32_t lo6, uint32_t idesc,
+                                              uint32_t acc0) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t.reg .b32 r, a1, a2, a3, a4;\n\t.reg .b64 b0, b1, b2, b3, b4, b5;\n\t"
+        "setp.ne.b32 p, %13, 0;\n\t"
+        "add.u32 a1, %1, 8;\n\tadd.u32 a2, %1, 16;\n\tadd.u32 a3, %1, 24;\n\tadd.u32 a4, %1, 32;\n\t"
+        "mov.b64 b0, {%2, %7};\n\tmov.b64 b1, {%3, %8};\n\tmov.b64 b2, {%4, %9};\n\t"
+        "mov.b64 b3, {%5, %10};\n\tmov.b64 b4, {%6, %11};\n\tmov.b64 b5, {%15, %16};\n\t"
+        "elect.sync r|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], b0, %12, p;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], b1, %12, 1;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], b2, %12, 1;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], b3, %12, 1;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a4], b4, %12, 1;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%14], b5, %12, 1;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "r"(lo[0]), "r"(lo[1]), "r"(lo[2]), "r"(lo[3]), "r"(lo[4]), "r"(hi[0]), "r"(hi[1]),
+        "r"(hi[2]), "r"(hi[3]), "r"(hi[4]), "r"(idesc), "r"(acc0), "r"(a6), "r"(lo6), "r"(kDescHiSW32)
+        : "memory");
+}
+
 // tcgen05.commit from a converged warp (one elected lane).
 __device__ __forceinline__ void tc_commit_warp(uint64_t* bar) {
     asm volatile(

@@ -90,7 +90,10 @@ struct Cfg {
     static constexpr int kRowBytes = kKB * T::kXElem;
     static constexpr int kWide = kRowBytes / 128;
     static constexpr int kTail = kRowBytes % 128;
-    static constexpr int kXDataBytes = kSlabBytes * T::kSteps;
+    // Decode stages carry one more slab: the k-block's offset correction (see
+    // permute_x_kernel), multiplied by constant A columns in one extra MMA.
+    static constexpr int kXSlabs = kPerm ? T::kSteps + 1 : T::kSteps;
+    static constexpr int kXDataBytes = kSlabBytes * kXSlabs;
     static constexpr int kXStageBytes = (kXDataBytes + 1023) / 1024 * 1024;
     static constexpr int kChunksPerRow = kKB * T::kXElem / 16;      // 16-byte pieces of one row per k-block
     static constexpr int kDCols = kIssuers * BT;                  // accumulators D_0..D_{kIssuers-1}
@@ -108,22 +111,24 @@ struct Cfg {
     static constexpr int kAParties = kUnpackGroups * T::kAPerKB;  // stage uses per round of groups
     static constexpr int kSAfit = (kTmemCols - kA0) / kAStageCols;
     static constexpr int kSA = (kSAfit >= 8 ? 8 : kSAfit) / kAParties * kAParties;
-    // A k-block's operand stages are released together, by one commit after
-    // its last MMA: one "slot" = kAPerKB consecutive stages.
-    static constexpr int kSlots = kSA / T::kAPerKB;
-    static constexpr int kBudget = 200 * 1024;
+    static constexpr int kBudget = 218 * 1024;
     static constexpr int kSW = kXStageBytes >= 40 * 1024 ? 4 : (kXStageBytes >= 20 * 1024 ? 6 : 8);
     static constexpr int kSXfit = (kBudget - kSW * kWStageBytes) / kXStageBytes;
-    static constexpr int kSX = (kSXfit > 8 ? 8 : kSXfit) / kIssuers * kIssuers;
+    // Up to three activation stages per issuer: a copy is issued when the
+    // stage's use kSX k-blocks earlier is done, so deeper rings hide its latency.
+    static constexpr int kSX = (kSXfit > 3 * kIssuers ? 3 * kIssuers : (kSXfit > 8 ? 8 : kSXfit)) / kIssuers * kIssuers;
     static constexpr int kBarOff = kSX * kXStageBytes + kSW * kWStageBytes;
-    static constexpr int kNumBars = 2 * kSW + 2 * kSX + 2 * kSA + 3 + kIssuers;
+    // TMEM columns holding the constant A operand of the correction MMA (decode)
+    static constexpr int kConstCol = kA0 + kSA * kAStageCols;
+    static constexpr int kNumBars = 2 * kSW + 2 * kSX + 2 * kSA + 4 + kIssuers;
     static constexpr int kSmem = kBarOff + kNumBars * 8 + 16 + 1024;  // + tmem slot, abort and last-arriver flags + align slack
     static_assert(kSX >= 2 && kSX % kIssuers == 0, "activation ring");
     static_assert(kSA >= kAParties && kSA % kAParties == 0 && kSA % (kIssuers * T::kAPerKB) == 0, "TMEM operand ring");
     static_assert(kSW % 2 == 0, "weight ring: two producers, two k-blocks per stage");
     static_assert((kSX * kXStageBytes) % 1024 == 0, "weight stages must stay 1024-byte aligned (128B swizzle)");
-    static_assert(kA0 + kSA * kAStageCols <= kTmemCols, "TMEM over-subscribed");
+    static_assert(kA0 + kSA * kAStageCols + (kPerm ? 8 : 0) <= kTmemCols, "TMEM over-subscribed");
     static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "token tile");
+    static_assert(kSmem <= 227 * 1024, "shared memory per block");
     static_assert(kTail == 32 || kTail == 64, "activation tail box");
 };
 
@@ -193,33 +198,33 @@ __device__ __forceinline__ void unpack_word_bf16(uint32_t p, uint32_t* r) {
     r[4] = bf16_pair(p >> 24, p >> 11);
 }
 
-// Decode variant: five bf16x2 registers per word in a permuted k order with
-// power-of-two scales, built from two right shifts, one left shift (an IMAD,
-// off the ALU pipe) and five mask-merges -- 0.7 ALU operations per weight
-// instead of ~2.  Register j holds codes j (low half) and j+5 (high half):
-// position 2j <- code j, position 2j+1 <- code j+5 of the word, and the value
-// stored at position q is (c - 2) * 2^kPermExp(q).  The activations are
-// permuted and scaled by 2^-kPermExp(q) to match (permute_x_kernel), so every
-// product is unchanged.
+// Decode variant: five bf16x2 registers per word in a permuted k order, each
+// half a bf16 subnormal c * 2^(j-133) holding the raw code c = q + 2 at
+// mantissa bit j -- two right shifts, one left shift (an IMAD, off the ALU
+// pipe) and five masks, 0.8 instructions per weight with no floating-point
+// work.  Register r holds codes r (low half) and r+5 (high half): position 2r
+// <- code r, position 2r+1 <- code r+5 of the word, and the value stored at
+// position q is c * 2^(kPermExp(q) - 133).  The activations are permuted to
+// match and scaled by 2^(66 - kPermExp(q)) (permute_x_kernel), so every
+// product is c * x * 2^-67 (exact: tcgen05 keeps bf16 subnormal operands),
+// and the offset of the code, sum_k -2 x_k per k-block, enters the
+// accumulator through one extra MMA per k-block (constant A columns times a
+// correction slab written by the pre-pass).
 __host__ __device__ constexpr int perm_src(int q) { return (q & 1) ? (q >> 1) + 5 : (q >> 1); }
 __host__ __device__ constexpr int perm_exp(int q) {
     return (int)((0x3401340101ull >> (4 * q)) & 0xF);  // {1,0,1,0,4,3,1,0,4,3}
 }
-__device__ __forceinline__ uint32_t bf16_sub2(uint32_t t, uint32_t c) {
-    uint32_t r;
-    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(t), "r"(c));
-    return r;
-}
+// Decode products accumulate in units of 2^-67 (the scales above).
+constexpr int kPermUnitExp = 67;
 __device__ __forceinline__ void unpack_word_bf16_perm(uint32_t p, uint32_t* r) {
     const uint32_t l1 = p * 2u;  // IMAD, not a shift
     const uint32_t r2 = p >> 2;
     const uint32_t r8 = p >> 8;
-    // (code j at bit o_lo, code j+5 at bit 16+o_hi) | bf16 128.0 in both halves
-    r[0] = bf16_sub2(and_or<0x0007000Eu, 0x43004300u>(l1), 0x43024304u);  // 132 lo, 130 hi
-    r[1] = bf16_sub2(and_or<0x0007000Eu, 0x43004300u>(r2), 0x43024304u);
-    r[2] = bf16_sub2(and_or<0x00380070u, 0x43004300u>(r2), 0x43104320u);  // 160 lo, 144 hi
-    r[3] = bf16_sub2(and_or<0x0007000Eu, 0x43004300u>(r8), 0x43024304u);
-    r[4] = bf16_sub2(and_or<0x00380070u, 0x43004300u>(r8), 0x43104320u);
+    r[0] = l1 & 0x0007000Eu;  // code 0 at bit 1, code 5 at bit 16
+    r[1] = r2 & 0x0007000Eu;  // code 1 at bit 1, code 6 at bit 16
+    r[2] = r2 & 0x00380070u;  // code 2 at bit 4, code 7 at bit 19
+    r[3] = r8 & 0x0007000Eu;  // code 3 at bit 1, code 8 at bit 16
+    r[4] = r8 & 0x00380070u;  // code 4 at bit 4, code 9 at bit 19
 }
 
 // Unsigned codes of two packed words (20 weights) as five int8x4 registers in
@@ -324,7 +329,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* acc_full = empty_a + C::kSA;
     uint64_t* acc_empty = acc_full + 1;
     uint64_t* drain = acc_empty + 1;  // one per issuer
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + C::kIssuers);
+    uint64_t* const_bar = drain + C::kIssuers;  // decode: constant A columns written
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(const_bar + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -352,6 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(acc_full, C::kIssuers);
         mbar_init(acc_empty, kUnpackWarps);
         for (int i = 0; i < C::kIssuers; ++i) mbar_init(&drain[i], 1);
+        mbar_init(const_bar, 4);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -400,24 +407,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == kXLoadWarp) {
         // -------------------------------------------- activation loader ----
-        // (decode tiles read the pre-pass's output: wait for that grid)
-        if (C::kPerm) asm volatile("griddepcontrol.wait;" ::: "memory");
-        uint32_t it = 0;
-        bool ok = true;
-        const int64_t u_end = range_begin(p, blockIdx.x + 1);
-        for (int64_t u = range_begin(p, blockIdx.x); u < u_end && ok;) {
-            const Seg g = segment_at(p, u, u_end);
-            u += (g.kb1 - g.kb0) / 2;
-            const int m0 = (g.tile / p.n_row_tiles) * BT;
-            for (int kb = g.kb0; kb < g.kb1; ++kb, ++it) {
-                const int sx = it % C::kSX;
-                if (!warp_wait(&empty_x[sx], ((it / C::kSX) & 1) ^ 1, abort_flag)) { ok = false; break; }
-                uint8_t* xs = smem_x + sx * C::kXStageBytes;
-                if (lane == 0) {
+        // One lane serves every issuer's activation stages.  Stage s belongs
+        // to issuer s mod kIssuers (k-block c of this CTA uses stage c mod kSX
+        // and issuer c mod kIssuers), and each issuer's stages are refilled as
+        // soon as its own MMAs release them: a slow issuer never holds back
+        // the copies of the others.
+        if (lane == 0) {
+            // (decode tiles read the pre-pass's output: wait for that grid)
+            if (C::kPerm) asm volatile("griddepcontrol.wait;" ::: "memory");
+            const int64_t u_begin = range_begin(p, blockIdx.x);
+            const uint32_t total = (uint32_t)(2 * (range_begin(p, blockIdx.x + 1) - u_begin));
+            const uint32_t P = (uint32_t)(p.n_kb / 2);
+            uint32_t cur[C::kIssuers];  // next k-block of each issuer
+#pragma unroll
+            for (int i = 0; i < C::kIssuers; ++i) cur[i] = i;
+            bool ok = true;
+            long long t_idle = clock64();
+            while (true) {
+                bool left = false, moved = false;
+#pragma unroll
+                for (int i = 0; i < C::kIssuers; ++i) {
+                    const uint32_t c = cur[i];
+                    if (c >= total) continue;
+                    left = true;
+                    const int sx = c % C::kSX;
+                    if (!mbar_test_wait(&empty_x[sx], ((c / C::kSX) & 1) ^ 1)) continue;
+                    // k-block c of the CTA's range: pair u, its tile and k-block index
+                    const uint32_t u = (uint32_t)u_begin + (c >> 1);
+                    const uint32_t tile = u / P;
+                    const int kb = (int)(2 * (u - tile * P) + (c & 1));
+                    uint8_t* xs = smem_x + sx * C::kXStageBytes;
                     mbar_arrive_expect_tx(&full_x[sx], C::kXDataBytes);
                     if constexpr (C::kPerm) {
                         bulk_load(xs, p.xperm + (size_t)kb * C::kXDataBytes, C::kXDataBytes, &full_x[sx]);
                     } else {
+                        const int m0 = (int)(tile / (uint32_t)p.n_row_tiles) * BT;
                         const int k0 = kb * kKB;
 #pragma unroll
                         for (int b = 0; b < C::kWide; ++b)
@@ -425,14 +449,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tma_load_2d(xs + C::kWide * BT * 128, &xmap_tail, &full_x[sx],
                                     k0 + C::kWide * (128 / T::kXElem), m0);
                     }
+                    cur[i] = c + C::kIssuers;
+                    moved = true;
                 }
-                __syncwarp();
+                if (!left) break;
+                if (moved) {
+                    t_idle = clock64();
+                    continue;
+                }
+                if (*abort_flag) {
+                    ok = false;
+                    break;
+                }
+                if (clock64() - t_idle > kWaitLimitCycles) {
+                    *abort_flag = 1;
+                    record_status(PN_ERR_TIMEOUT);
+                    ok = false;
+                    break;
+                }
+                // Nothing free: sleep on the stage of the oldest pending k-block
+                // (the next one the MMAs release) instead of polling, which would
+                // take issue slots from the unpack warps of this sub-partition.
+                uint32_t oldest = 0xffffffffu;
+#pragma unroll
+                for (int i = 0; i < C::kIssuers; ++i)
+                    if (cur[i] < total && cur[i] < oldest) oldest = cur[i];
+                mbar_try_wait(&empty_x[oldest % C::kSX], ((oldest / C::kSX) & 1) ^ 1);
             }
-        }
-        if (!ok && lane == 0) {
-            // Let every issued copy land before the CTA can exit.
-            const uint32_t first = it > (uint32_t)C::kSX ? it - C::kSX : 0u;
-            for (uint32_t j = first; j < it; ++j) mbar_wait_drain(&full_x[j % C::kSX], (j / C::kSX) & 1);
+            if (!ok) {
+                // Let every issued copy land before the CTA can exit: an issuer's
+                // copies in flight are its last kSX / kIssuers ones.
+#pragma unroll 1
+                for (int i = 0; i < C::kIssuers; ++i)
+                    for (uint32_t c = cur[i] >= (uint32_t)C::kSX ? cur[i] - C::kSX : (uint32_t)i; c < cur[i];
+                         c += C::kIssuers)
+                        mbar_wait_drain(&full_x[c % C::kSX], (c / C::kSX) & 1);
+            }
         }
     } else if (warp >= kMmaWarp) {
         // --------------------------------------------------------- MMAs ----
@@ -449,6 +501,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t d_tmem = tmem_base + issuer * BT;
             uint32_t it = 0, n_local = 0;
             bool ok = true;
+            if constexpr (C::kPerm) {
+                ok = warp_wait(const_bar, 0, abort_flag);
+                tc_fence_after();
+            }
             const int64_t u_end = range_begin(p, blockIdx.x + 1);
             for (int64_t u = range_begin(p, blockIdx.x); u < u_end && ok; ++n_local) {
                 const Seg g = segment_at(p, u, u_end);
@@ -491,11 +547,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 hi[j] = kDescHiSW64;
                             }
                         }
-                        mma5_ts_warp<KIND == Kind::I8>(d_tmem, a_col, lo, hi, idesc, first ? 0u : 1u);
+                        if (C::kPerm && hh == T::kAPerKB - 1) {
+                            // + the k-block's offset correction: constant A columns x slab kSteps
+                            mma5c_ts_warp(d_tmem, a_col, lo, hi, tmem_base + C::kConstCol,
+                                          xs_lo + ((T::kSteps * C::kSlabBytes) >> 4), idesc, first ? 0u : 1u);
+                        } else {
+                            mma5_ts_warp<KIND == Kind::I8>(d_tmem, a_col, lo, hi, idesc, first ? 0u : 1u);
+                        }
                         first = false;
+                        // the stage is free for its group once these MMAs are done
+                        tc_commit_warp(&empty_a[sa]);
                     }
                     if (!ok) break;
-                    tc_commit_warp(&empty_a[ik % C::kSlots]);
                     tc_commit_warp(&empty_x[sx]);
                 }
                 it = it0 + nkb;
@@ -522,6 +585,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int half = warp >> 2;  // warp group within the quarter
         const int row = quarter * 32 + lane;
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+        if constexpr (C::kPerm) {
+            // Constant A operand of the correction MMA: 1.0 at K positions 0-2
+            // of every row (bf16 pairs: column 0 = (1, 1), column 1 = (1, 0)).
+            if (half == 0) {
+                const uint32_t one[8] = {0x3F803F80u, 0x00003F80u, 0u, 0u, 0u, 0u, 0u, 0u};
+                tmem_st8(tmem_base + lane_base + C::kConstCol, one);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(const_bar);
+            }
+        }
         uint32_t it = 0, n_local = 0;
         bool ok = true;
         const int64_t u_begin = range_begin(p, blockIdx.x);
@@ -571,14 +646,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     const uint32_t ua = ik * T::kAPerKB + hh;  // operand stage use
                     const int sa = ua % C::kSA;
-                    if (hh == 0) {
-                        // the k-block's slot is free once the MMAs of its previous use are done
-                        if (!warp_wait(&empty_a[ik % C::kSlots], ((ik / C::kSlots) & 1) ^ 1, abort_flag)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                    }
                     const uint32_t a_addr = tmem_base + lane_base + C::kA0 + sa * C::kAStageCols;
                     uint32_t cols[40];
                     if constexpr (KIND == Kind::F16) {
@@ -598,6 +665,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                             unpack_pair_u8(wb[2 * w], wb[2 * w + 1], &cols[20 + 5 * w]);
                         }
                     }
+                    // The stage is free once the MMAs of its previous use are done
+                    // (waited after the unpack, so that the ALU work overlaps them).
+                    // Every stage belongs to one group (stage = 2 * (k-block mod 4) + half
+                    // for bf16, k-block mod 8 for int8), so the group sees each of its
+                    // phases in order.
+                    if (!warp_wait(&empty_a[sa], ((ua / C::kSA) & 1) ^ 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
 #pragma unroll
                     for (int c = 0; c < 5; ++c) {
                         uint32_t v8[8];
@@ -628,6 +705,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int64_t n = n0 + row;
             float bias_f = 0.0f;
             if (p.bias != nullptr && n < p.N) bias_f = __bfloat162float(p.bias[n]);
+            // bf16 products: decode accumulators are in units of 2^-67; the
+            // power-of-two rescale is exact, so acc * scale is rounded once.
+            auto f16_out = [&](uint32_t a) {
+                float v = __uint_as_float(a);
+                if constexpr (C::kPerm) v = __fmul_rn(v, 0x1p67f);
+                return __fmul_rn(v, p.scale);
+            };
+            // Fixed-point unit of the split-tile sums (2^-24 of an output unit).
+            constexpr float kFix = C::kPerm ? 0x1p91f : kFixScale;
             // Final epilogue of 16 accumulator columns starting at c0.
             // MULTI: output-sharded layers store into every GPU's buffer; the
             // common single-output case is compiled separately.
@@ -640,7 +726,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (m >= p.M) break;
                     float yv;
                     if constexpr (KIND == Kind::F16) {
-                        yv = __fmul_rn(__uint_as_float(acc[j]), p.scale);
+                        yv = f16_out(acc[j]);
                     } else {
                         const int acc_i = (int)acc[j] - 2 * __ldg(p.rowsum + m);
                         if (p.acc_out) p.acc_out[(int64_t)m * p.N + n] = acc_i;
@@ -683,7 +769,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < 16; ++j) {
                     float yv;
                     if constexpr (KIND == Kind::F16) {
-                        yv = __fmul_rn(__uint_as_float(acc[j]), p.scale);
+                        yv = f16_out(acc[j]);
                     } else {
                         const int m = m0 + c0 + j;
                         const int acc_i = (int)acc[j] - 2 * __ldg(p.rowsum + m);
@@ -701,7 +787,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < 16; ++j) {
                     float yv;
                     if constexpr (KIND == Kind::F16) {
-                        yv = __fmul_rn(__uint_as_float(acc[j]), p.scale);
+                        yv = f16_out(acc[j]);
                     } else {
                         const int m = m0 + c0 + j;
                         const int acc_i = (int)acc[j] - 2 * __ldg(p.rowsum + m);
@@ -737,7 +823,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = j0; j < j0 + 8; ++j) {
                         float yv;
                         if constexpr (KIND == Kind::F16) {
-                            yv = __fmul_rn(__uint_as_float(acc[j]), p.scale);
+                            yv = f16_out(acc[j]);
                         } else {
                             const int m = m0 + c0 + j;
                             const int acc_i = (int)acc[j] - 2 * __ldg(p.rowsum + m);
@@ -808,7 +894,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (m0 + c0 + j >= p.M) break;
                         if constexpr (KIND == Kind::F16)
                             red_add(static_cast<long long*>(p.accbuf) + acc_base + (size_t)(c0 + j) * kRows,
-                                    __float2ll_rn(__uint_as_float(acc[j]) * kFixScale));
+                                    __float2ll_rn(__uint_as_float(acc[j]) * kFix));
                         else
                             red_add(static_cast<int*>(p.accbuf) + acc_base + (size_t)(c0 + j) * kRows, (int)acc[j]);
                     }
@@ -853,7 +939,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     if constexpr (KIND == Kind::F16) {
                                         const long long v =
                                             __ldcg(static_cast<const long long*>(p.accbuf) + acc_base + (size_t)(c0 + j) * kRows);
-                                        acc[j] = __float_as_uint(__ll2float_rn(v) * (1.0f / kFixScale));
+                                        acc[j] = __float_as_uint(__ll2float_rn(v) * (1.0f / kFix));
                                     } else {
                                         acc[j] = (uint32_t)__ldcg(static_cast<const int*>(p.accbuf) + acc_base + (size_t)(c0 + j) * kRows);
                                     }
@@ -905,9 +991,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Writes the activations of a bf16 decode tile as the GEMM kernel's shared-
 // memory image of its B operand: per k-block 10 slabs (MMA K-steps) of BT rows
 // x 32 bytes, 32-byte swizzled, each 10-group of k permuted by perm_src and
-// scaled by 2^-perm_exp (exact).  Positions past K are zero; rows >= M are not
-// written (their accumulator columns are never read back).
-constexpr int kPermThreads = 256;
+// scaled by 2^(133 - 67 - perm_exp) (exact), then an 11th slab holding the
+// k-block's offset correction: the weights enter the MMAs as their codes
+// c = q + 2, so sum_k q x = sum_k c x - 2 sum_k x, and per token the value
+// t = -2 * 2^-67 * sum_k x (the sum over the k-block, in fp32, in a fixed
+// order) is stored as three bf16 pieces (t = p1 + p2 + p3 exactly) at K
+// positions 0-2, which the kernel multiplies by constant 1.0 A columns.
+// Positions past K are zero; rows >= M are not written (their accumulator
+// columns are never read back).
+//
+// One block per (token, k-block) at a time, one thread per position of the
+// k-block (160 threads, five warps): every thread loads, scales and stores one
+// value, and the k-block's sum is a fixed-order reduction (a shuffle tree per
+// warp, then the five warp sums in order), so the result is deterministic.
+constexpr int kPermThreads = kKB;
 template <int BT>
 __global__ void __launch_bounds__(kPermThreads) permute_x_kernel(const __nv_bfloat16* __restrict__ x, int M, int64_t K,
                                                         int n_kb, uint8_t* __restrict__ out, uint4* __restrict__ zero,
@@ -916,33 +1013,53 @@ __global__ void __launch_bounds__(kPermThreads) permute_x_kernel(const __nv_bflo
     // start its prologue and weight streaming now; it waits for this grid's
     // results before it reads them.
     asm volatile("griddepcontrol.launch_dependents;");
-    // This grid may itself be a programmatic dependent of the previous product
-    // on the stream (whose output can be this x, and whose workspace this one
-    // can reuse): nothing is read or written before that grid has completed.
-    asm volatile("griddepcontrol.wait;" ::: "memory");
     // the GEMM's split-tile counters and sums start at zero
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_zero16; i += (int64_t)gridDim.x * blockDim.x)
         zero[i] = make_uint4(0, 0, 0, 0);
-    // 32-bit index arithmetic (the host checks M * n_kb * 160 < 2^31): this
-    // grid runs beside the GEMM's unpack warps and should take few of their
-    // issue slots.
-    const uint32_t kpad = (uint32_t)n_kb * kKB;
-    const uint32_t total = (uint32_t)M * kpad;
-    for (uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
-        const uint32_t m = idx / kpad;
-        const uint32_t kk = idx - m * kpad;
-        const uint32_t g = kk / kPerWord;
-        const int q = (int)(kk - g * kPerWord);
-        const uint32_t ksrc = g * kPerWord + perm_src(q);
-        float v = ksrc < (uint64_t)K ? __bfloat162float(x[(int64_t)m * K + ksrc]) : 0.0f;
-        v = __fmul_rn(v, __int_as_float((127 - perm_exp(q)) << 23));  // * 2^-perm_exp(q), exact
-        const uint32_t kb = kk / kKB;
-        const uint32_t e = kk - kb * kKB;
-        const uint32_t j = e >> 4;
-        const uint32_t ee = e & 15;
-        const uint32_t h = (ee >> 3) ^ ((m >> 2) & 1);
-        const size_t off = (size_t)kb * (BT * 32 * 10) + j * BT * 32 + m * 32 + h * 16 + (ee & 7) * 2;
-        *reinterpret_cast<__nv_bfloat16*>(out + off) = __float2bfloat16_rn(v);
+    constexpr int kStage = BT * 32 * 11;
+    __shared__ float warp_sum[kPermThreads / 32];
+    const uint32_t e = threadIdx.x;  // position in the k-block
+    const uint32_t grp = e / kPerWord;
+    const int q = (int)(e - grp * kPerWord);
+    const uint32_t src = grp * kPerWord + perm_src(q);
+    const uint32_t j = e >> 4, ee = e & 15;
+    // * 2^(133 - 67 - perm_exp(q)), exact
+    const float vscale = __int_as_float((127 + 133 - kPermUnitExp - perm_exp(q)) << 23);
+    // 32-bit index arithmetic (the host checks M * n_kb * 160 < 2^31)
+    const uint32_t pairs = (uint32_t)M * (uint32_t)n_kb;
+    for (uint32_t mk = blockIdx.x; mk < pairs; mk += gridDim.x) {
+        const uint32_t m = mk / (uint32_t)n_kb;
+        const uint32_t kb = mk - m * (uint32_t)n_kb;
+        uint8_t* const kbase = out + (size_t)kb * kStage + m * 32;
+        const uint32_t flip = (m >> 2) & 1;  // 32-byte swizzle: 16-byte halves swap every 4 rows
+        const uint32_t ksrc = kb * kKB + src;
+        const float v = ksrc < (uint64_t)K ? __bfloat162float(x[(size_t)m * K + ksrc]) : 0.0f;
+        *reinterpret_cast<__nv_bfloat16*>(kbase + j * (BT * 32) + (((ee >> 3) ^ flip) << 4) + (ee & 7) * 2) =
+            __float2bfloat16_rn(__fmul_rn(v, vscale));
+        float sum = v;
+        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 16));
+        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 8));
+        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 4));
+        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 2));
+        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 1));
+        if ((e & 31) == 0) warp_sum[e >> 5] = sum;
+        __syncthreads();
+        if (e == 0) {
+            float t = warp_sum[0];
+#pragma unroll
+            for (int w = 1; w < kPermThreads / 32; ++w) t = __fadd_rn(t, warp_sum[w]);
+            t = __fmul_rn(t, -0x1p-66f);  // -2 * 2^-67 * sum, exact
+            const __nv_bfloat16 p1 = __float2bfloat16_rn(t);
+            const float r1 = __fsub_rn(t, __bfloat162float(p1));
+            const __nv_bfloat16 p2 = __float2bfloat16_rn(r1);
+            const __nv_bfloat16 p3 = __float2bfloat16_rn(__fsub_rn(r1, __bfloat162float(p2)));
+            const uint32_t w01 = (uint32_t)__bfloat16_as_ushort(p1) | ((uint32_t)__bfloat16_as_ushort(p2) << 16);
+            const uint32_t w23 = (uint32_t)__bfloat16_as_ushort(p3);
+            uint8_t* const slab = kbase + 10 * (BT * 32);
+            *reinterpret_cast<uint4*>(slab + (flip << 4)) = make_uint4(w01, w23, 0u, 0u);       // K 0-7
+            *reinterpret_cast<uint4*>(slab + ((flip ^ 1) << 4)) = make_uint4(0u, 0u, 0u, 0u);  // K 8-15
+        }
+        __syncthreads();  // warp_sum is reused by the next pair
     }
 }
 
@@ -1008,7 +1125,9 @@ struct WsLayout {
     int64_t n_items, total_pairs;
     int grid, bt, n_kb, unit, acc_cols;
 };
-static WsLayout ws_layout(int kind, int64_t M, int64_t N, int64_t K, bool allow_split) {
+// repitch: the packed rows are not 16 bytes apart (packed_ld % 4 != 0), so a
+// 16-byte-pitch copy of the whole matrix is part of the workspace.
+static WsLayout ws_layout(int kind, int64_t M, int64_t N, int64_t K, bool allow_split, bool repitch) {
     WsLayout w{};
     const int64_t KP = (K + kPerWord - 1) / kPerWord;
     w.bt = token_tile(kind, M);
@@ -1023,9 +1142,9 @@ static WsLayout ws_layout(int kind, int64_t M, int64_t N, int64_t K, bool allow_
     w.grid = (int)(units < sms ? units : sms);
     size_t off = 0;
     w.xperm = off;
-    if (kind == PN_BF16 && M >= 1 && M <= 64) off += round256((size_t)w.n_kb * w.bt * 32 * 10);
+    if (kind == PN_BF16 && M >= 1 && M <= 64) off += round256((size_t)w.n_kb * w.bt * 32 * 11);
     w.wpitch = off;
-    if (KP % 4 != 0) off += round256((size_t)N * w_pitch(KP) * 4);
+    if (repitch) off += round256((size_t)N * w_pitch(KP) * 4);
     w.acc_cols = (int)(M < 16 ? M : 16);
     w.counters = off;
     w.accbuf = off;
@@ -1044,13 +1163,13 @@ static WsLayout ws_layout(int kind, int64_t M, int64_t N, int64_t K, bool allow_
     w.total = off;
     return w;
 }
-size_t linear_workspace_bytes(int kind, int64_t M, int64_t N, int64_t K) {
+size_t linear_workspace_bytes(int kind, int64_t M, int64_t N, int64_t K, int64_t packed_ld) {
     if (M <= 0 || N <= 0) return 0;
-    return ws_layout(kind, M, N, K, true).total;
+    return ws_layout(kind, M, N, K, true, packed_ld % 4 != 0).total;
 }
-size_t linear_workspace_min_bytes(int kind, int64_t M, int64_t N, int64_t K) {
+size_t linear_workspace_min_bytes(int kind, int64_t M, int64_t N, int64_t K, int64_t packed_ld) {
     if (M <= 0 || N <= 0) return 0;
-    return ws_layout(kind, M, N, K, false).total;
+    return ws_layout(kind, M, N, K, false, packed_ld % 4 != 0).total;
 }
 
 // Copies packed rows (src_ld words apart) into a 16-byte pitch so that TMA
@@ -1104,8 +1223,12 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     // x 32 words).  TMA needs 16-byte row pitches; other shapes are first copied
     // into the workspace with the pitch rounded up.
     // The full layout when the workspace holds it, else whole tiles per CTA.
-    WsLayout L = ws_layout(a.kind, a.M, a.N, a.K, true);
-    if (a.workspace_bytes < L.total) L = ws_layout(a.kind, a.M, a.N, a.K, false);
+    // TMA reads the rows in place when they are 16 bytes apart (a multiple of
+    // 4 words: K_packs % 4 == 0, or rows stored at a padded stride); other
+    // layouts are first copied into the workspace at a 16-byte pitch.
+    const bool repitch = a.packed_ld % 4 != 0;
+    WsLayout L = ws_layout(a.kind, a.M, a.N, a.K, true, repitch);
+    if (a.workspace_bytes < L.total) L = ws_layout(a.kind, a.M, a.N, a.K, false, repitch);
     if (L.bt != BT) {
         *why = "internal: token tile mismatch";
         return PN_ERR_ARG;
@@ -1116,10 +1239,6 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
         return PN_ERR_WORKSPACE;
     }
     uint8_t* ws = static_cast<uint8_t*>(a.workspace);
-    // TMA reads the rows in place when they are 16 bytes apart (a multiple of
-    // 4 words: K_packs % 4 == 0, or rows stored at a padded stride); other
-    // layouts are first copied into the workspace at a 16-byte pitch.
-    const bool repitch = a.packed_ld % 4 != 0;
     const int64_t pitch = repitch ? w_pitch(a.KP) : a.packed_ld;
     const int32_t* wsrc = a.packed;
     if (repitch) {
@@ -1171,32 +1290,18 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
             *why = "activation re-layout exceeds 32-bit indexing (K too large)";
             return PN_ERR_UNSUPPORTED;
         }
-        int64_t want = (total + kPermThreads - 1) / kPermThreads;
+        // one block per (token, k-block); extra blocks when the zeroing needs them
+        int64_t want = a.M * (int64_t)prm.n_kb;
         if (n_zero16 / (4 * kPermThreads) > want) want = n_zero16 / (4 * kPermThreads);  // ~4 zeroing stores per thread
-        const int blocks = (int)(want < 1024 ? (want > 0 ? want : 1) : 1024);
+        const int blocks = (int)(want < 4096 ? (want > 0 ? want : 1) : 4096);
         const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(a.x);
         uint4* zero = reinterpret_cast<uint4*>(ws + L.counters);
-        cudaError_t e;
-        if (!repitch) {
-            // a programmatic dependent of the previous kernel on the stream
-            // (the kernel waits for it before touching memory); with a
-            // re-pitched weight copy the GEMM's weight loads depend on the
-            // copy kernel, so then the launch is fully serialised
-            cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3(blocks);
-            cfg.blockDim = dim3(kPermThreads);
-            cfg.stream = s;
-            cudaLaunchAttribute attr[1];
-            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-            attr[0].val.programmaticStreamSerializationAllowed = 1;
-            cfg.attrs = attr;
-            cfg.numAttrs = 1;
-            e = cudaLaunchKernelEx(&cfg, permute_x_kernel<BT>, xb, (int)a.M, a.K, prm.n_kb, ws + L.xperm, zero,
-                                   n_zero16);
-        } else {
-            permute_x_kernel<BT><<<blocks, kPermThreads, 0, s>>>(xb, (int)a.M, a.K, prm.n_kb, ws + L.xperm, zero, n_zero16);
-            e = cudaGetLastError();
-        }
+        // A plain launch: it runs once everything before it on the stream is
+        // done (its x may be the previous product's output, and its workspace
+        // the previous product's), on SMs no GEMM occupies yet, so it is short;
+        // the GEMM after it is its programmatic dependent.
+        permute_x_kernel<BT><<<blocks, kPermThreads, 0, s>>>(xb, (int)a.M, a.K, prm.n_kb, ws + L.xperm, zero, n_zero16);
+        cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) {
             *err = e;
             *why = "activation re-layout launch";

@@ -48,9 +48,10 @@ struct LinearArgs {
     size_t workspace_bytes;
 };
 // Workspace that lets tiles split across SMs (recommended), and the least the
-// kernel runs with (whole tiles per SM).
-size_t linear_workspace_bytes(int kind, int64_t M, int64_t N, int64_t K);
-size_t linear_workspace_min_bytes(int kind, int64_t M, int64_t N, int64_t K);
+// kernel runs with (whole tiles per SM), for packed rows packed_ld words apart
+// (a re-pitched copy of the weights is included when packed_ld % 4 != 0).
+size_t linear_workspace_bytes(int kind, int64_t M, int64_t N, int64_t K, int64_t packed_ld);
+size_t linear_workspace_min_bytes(int kind, int64_t M, int64_t N, int64_t K, int64_t packed_ld);
 // Returns a pn_status_code; CUDA errors are reported through *cuda_err.
 int launch_linear(const LinearArgs& a, cudaStream_t s, cudaError_t* cuda_err, const char** why);
 

@@ -72,7 +72,7 @@ def load() -> ctypes.CDLL:
         "pn_linear_bf16_ld": (I, [P, I64, I64, P, I64, I64, I64, F, P, P, I, P, SZ, P]),
         "pn_linear_bf16_epi": (I, [P, I64, I64, P, I64, I64, I64, F, P, I, P, I64, P, I, P, SZ, P]),
         "pn_packed_ld": (I64, [I64]),
-        "pn_linear_bf16_nows": (I, [P, I64, I64, P, I64, I64, F, P, P, I, P]),
+        "pn_linear_bf16_nows": (I, [P, I64, I64, P, I64, I64, I64, F, P, P, I, P]),
         "pn_act_i8_pitch": (I64, [I64]),
         "pn_quant_act_i8": (I, [P, I, I64, I64, P, I64, P, P, P]),
         "pn_linear_i8": (I, [P, I64, P, P, I64, I64, P, I64, I64, F, P, P, I, P, P, SZ, P]),
