@@ -14,9 +14,12 @@ bytes per product) divided by device time.
 from source into oracle/_ref/, or the oracle port when it is absent) on the
 same workload with all host threads, on a bounded row sample per step.
 
-At N > 1 (torchrun) every layer is sharded by output rows over the ranks and
-each product ends in an NCCL all-gather of the output shards (strong scaling:
-the total work is fixed).
+At N > 1 (torchrun) every layer is sharded by output rows over the ranks: each
+rank's GEMM stores its output columns straight into every GPU's full-output
+buffer (CUDA IPC peer mappings over NVLink) and a cross-GPU barrier kernel
+ends each product, so every GPU holds the whole output (strong scaling: the
+total work is fixed).  The sharded outputs are checked against the unsharded
+product on every rank.
 
 The printed JSON line carries the device-timed value, an end-to-end number
 through the public API with host buffers, the roofline of the dqmm kernel, a
@@ -80,25 +83,43 @@ def measured_peaks() -> dict:
     return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
+def kernel_source_sha() -> str:
+    """sha256 of the decode GEMM's sources (the kernel an ncu capture describes)."""
+    import hashlib
+    h = hashlib.sha256()
+    for f in ("pn_dqmm.cu", "pn_common.cuh"):
+        with open(os.path.join(PKG, "csrc", f), "rb") as fh:
+            h.update(fh.read())
+    return h.hexdigest()[:16]
+
+
 def profile_traffic():
-    """dram bytes per launch of the dqmm kernel from the committed ncu summary."""
+    """DRAM bytes per launch of the dqmm kernel from the committed ncu summary,
+    used only when the summary was captured from the current kernel source
+    (its `kernel_source_sha:` line); returns (bytes or None, source note)."""
     path = os.path.join(ROOT, "profiles", "dqmm_gemv_70b_decode.md")
     if not os.path.exists(path):
-        return None
+        return None, "no ncu summary"
+    traffic = sha = None
     for line in open(path):
         if line.startswith("traffic_bytes_per_launch_full_size:"):
             try:
-                return float(line.split(":", 1)[1].strip())
+                traffic = float(line.split(":", 1)[1].strip())
             except ValueError:
-                return None
-    return None
+                traffic = None
+        if line.startswith("kernel_source_sha:"):
+            sha = line.split(":", 1)[1].strip()
+    if sha != kernel_source_sha():
+        return None, "profiles/dqmm_gemv_70b_decode.md was captured from another kernel source: not used"
+    return traffic, f"ncu capture of this kernel source ({sha}), profiles/dqmm_gemv_70b_decode.md"
 
 
 # --------------------------------------------------------------- clocks ----
 
 class ClockSampler:
-    """Samples SM clock, power and throttle reasons with NVML (every ~5 ms)
-    while the timed region runs."""
+    """Samples SM clock and throttle reasons with NVML (every ~1 ms) from the
+    start of the warm-up to the end of the per-launch timing; `window` marks
+    the timed region so the summary can say how many samples fell inside it."""
 
     def __init__(self, device_indices):
         self.samples = []
@@ -126,7 +147,7 @@ class ClockSampler:
                     self.samples.append((time.time(), sm, reasons))
                 except Exception:
                     pass
-            time.sleep(0.005)
+            time.sleep(0.001)
 
     def start(self):
         if self.ok:
@@ -137,6 +158,8 @@ class ClockSampler:
         if self._th:
             self._stop.set()
             self._th.join()
+
+    window = None
 
     def summary(self):
         if not self.ok or not self.samples:
@@ -155,23 +178,62 @@ class ClockSampler:
             for k, bit in names.items():
                 if k != "gpu_idle" and r & bit:
                     seen.add(k)
+        inside = [s for t, s, _ in self.samples if self.window and self.window[0] <= t <= self.window[1]]
         return {"sm_mhz": statistics.median(s for _, s, _ in self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(seen), "samples": len(self.samples)}
+                "reasons": sorted(seen), "samples": len(self.samples),
+                "samples_in_timed_region": len(inside),
+                "sm_mhz_timed_region": statistics.median(inside) if inside else None,
+                "sampled": "warm-up, timed region and per-launch timing, every ~1 ms"}
 
 
 # ------------------------------------------------------- CPU reference -----
 
-def cpu_reference_rate(sample_rows: int, reps: int, warmup: int, seed: int = 0):
+def host_cpu() -> dict:
+    """Host CPU facts recorded beside every CPU number."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    return {"cpu_model": model, "affinity_cores": cores, "env_OMP_NUM_THREADS": os.environ.get("OMP_NUM_THREADS")}
+
+
+def _timed_reps(fn, reps: int, warmup: int, budget_s: float):
+    """Run fn `warmup` times, then up to `reps` times or until budget_s has
+    passed (at least once); returns (seconds per rep, reps run)."""
+    for _ in range(warmup):
+        fn()
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        fn()
+        n += 1
+        dt = time.perf_counter() - t0
+        if n >= reps or dt >= budget_s:
+            return dt / n, n
+
+
+def cpu_reference_rate(sample_rows: int, reps: int, warmup: int, seed: int = 0, budget_s: float = 20.0):
     """The reference's CPU kernel (penta_matmul_avx2 over int8 weights from
     penta_unpack_3bit, as penta_avx2_wrapper.py:37-94 runs it) on the six
-    products, restricted to the first `sample_rows` output rows of each layer.
-    Returns (GB/s of algorithmic bytes, seconds per sample, kind, cores, desc)."""
+    products, restricted to the first `sample_rows` output rows of each layer,
+    with every host core the process may use (OpenMP threads set explicitly:
+    launchers such as torchrun export OMP_NUM_THREADS=1).
+    Returns a dict: value (GB/s of algorithmic bytes), seconds per sample,
+    kind, cores (threads used), sample description, reps, host facts."""
     import numpy as np
     import torch
     from oracle import oracle as orc
 
     kind = "reference" if orc.ref_avx2_available() else "port"
-    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    host = host_cpu()
+    cores = host["affinity_cores"]
+    threads = orc.ref_omp_threads(cores) if kind == "reference" else 1
     g = torch.Generator().manual_seed(seed)
     layers = {}
     for (K, N) in SHAPES:
@@ -179,29 +241,97 @@ def cpu_reference_rate(sample_rows: int, reps: int, warmup: int, seed: int = 0):
         w = (torch.randn(n, K, generator=g) * 0.02).numpy()
         packed, _, gamma = orc.quantize_pack(w)
         w8 = orc.ref_avx2_unpack(packed, K) if kind == "reference" else orc.unpack(packed, K)
-        layers[(K, N)] = (w8, gamma, n)
+        layers[(K, N)] = (w8, gamma, n, packed)
     xs = {(M, K): torch.randn(M, K, generator=g).to(torch.bfloat16).float().numpy()
           for (M, K, _) in launches_per_step()}
     outs = {(M, K, N): np.empty((M, layers[(K, N)][2]), dtype=np.float32) for (M, K, N) in launches_per_step()}
 
     def one():
         for (M, K, N) in launches_per_step():
-            w8, gamma, n = layers[(K, N)]
+            w8, gamma, n, _ = layers[(K, N)]
             if kind == "reference":
                 orc.ref_avx2_linear(xs[(M, K)], w8, gamma, outs[(M, K, N)])
             else:
                 outs[(M, K, N)][...] = orc.matmul_f32(xs[(M, K)], w8, gamma)
 
-    for _ in range(warmup):
-        one()
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        one()
-    dt = (time.perf_counter() - t0) / reps
+    dt, n_reps = _timed_reps(one, reps, warmup, budget_s)
     sample_bytes = sum(alg_bytes(M, K, layers[(K, N)][2]) for (M, K, N) in launches_per_step())
     desc = (f"rows 0..{sample_rows} of each layer (of 28672 / 8192), all six (shape, M) products per step; "
-            f"{'penta_matmul_avx2 (-O3 -mavx2 -mfma -fopenmp)' if kind == 'reference' else 'scalar oracle port'}")
-    return sample_bytes / dt / 1e9, dt, kind, cores, desc
+            f"{'penta_matmul_avx2 (-O3 -mavx2 -mfma -fopenmp)' if kind == 'reference' else 'scalar oracle port'}"
+            f"; {n_reps} timed reps after {warmup} warm-up")
+    res = {"value": round(sample_bytes / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+           "sample": desc, "s_per_sample": round(dt, 4), "reps": n_reps,
+           "threads": {"omp_max_threads": threads, "torch": torch.get_num_threads()}, **host}
+    return res, layers, xs
+
+
+def cpu_numba_rate(layers, xs, reps: int, warmup: int, budget_s: float = 10.0):
+    """The reference's numba kernel (penta_linear_cpu, penta_kernel_cpu.py:63-101,
+    restated in oracle/numba_port.py: per-call unpack of the packed words, then
+    the five-way add/subtract loop parallel over output rows) on the same
+    sample as the AVX2 leg, all host cores."""
+    import torch
+    from oracle import numba_port as nbp
+    if not nbp.AVAILABLE:
+        return {"unavailable": "numba not importable"}
+    threads = nbp.threads(host_cpu()["affinity_cores"])
+    tl = {k: torch.from_numpy(v[3]) for k, v in layers.items()}
+    tx = {k: torch.from_numpy(v) for k, v in xs.items()}
+
+    def one():
+        for (M, K, N) in launches_per_step():
+            nbp.penta_linear_cpu(tx[(M, K)], tl[(K, N)], layers[(K, N)][1], K)
+
+    one()  # JIT compile (and warm-up) outside the timing
+    dt, n_reps = _timed_reps(one, reps, 0, budget_s)
+    sample_bytes = sum(alg_bytes(M, K, layers[(K, N)][2]) for (M, K, N) in launches_per_step())
+    return {"value": round(sample_bytes / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": "same rows and products as the AVX2 leg; numba restatement of penta_linear_cpu "
+                      f"(per-call unpack included); {n_reps} timed reps",
+            "s_per_sample": round(dt, 4)}
+
+
+def cpu_int_mm_rate(reps: int, warmup: int, rows: int = 512, budget_s: float = 10.0):
+    """The reference's CPU int8 line for the 7B-class prefill shapes
+    (penta_avx2_wrapper.py:130-131,137,147: torch._int_mm of per-tensor int8
+    activations and int8 weights, then the float rescale) at M = 4096 on the
+    first `rows` output rows of each layer; TOP/s of 2*M*rows*K."""
+    import torch
+    threads = torch.get_num_threads()
+    torch.set_num_threads(host_cpu()["affinity_cores"])
+    g = torch.Generator().manual_seed(5)
+    cases = []
+    for (K, N) in PREFILL_SHAPES:
+        x = torch.randn(PREFILL_M, K, generator=g)
+        w8 = torch.randint(-2, 3, (rows, K), generator=g, dtype=torch.int8)
+        xs = x.abs().max() / 127.0
+        x8 = (x / xs).round().clamp(-128, 127).to(torch.int8)
+        cases.append((x8, w8.t(), float(xs) * 0.02))
+
+    def one():
+        for (x8, wt, sc) in cases:
+            torch._int_mm(x8, wt).float() * sc
+
+    try:
+        dt, n_reps = _timed_reps(one, reps, warmup, budget_s)
+    except RuntimeError as e:  # no CPU _int_mm kernel in this torch build
+        torch.set_num_threads(threads)
+        return {"unavailable": str(e).splitlines()[0][:200]}
+    ops = sum(2.0 * PREFILL_M * rows * K for (K, N) in PREFILL_SHAPES)
+    used = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    return {"value": round(ops / dt / 1e12, 4), "unit": "TOP/s", "cores": used, "kind": "port",
+            "sample": f"M={PREFILL_M}, first {rows} output rows of 4096->4096, 4096->11008, 11008->4096; "
+                      f"torch._int_mm as penta_avx2_wrapper.py runs it; {n_reps} timed reps",
+            "s_per_sample": round(dt, 4)}
+
+
+def cpu_legs(reps: int, warmup: int) -> dict:
+    rows = int(os.environ.get("PN_REF_ROWS", "2048"))
+    res, layers, xs = cpu_reference_rate(rows, reps, warmup)
+    res["legs"] = {"numba_penta_linear_cpu": cpu_numba_rate(layers, xs, reps, warmup),
+                   "int_mm_prefill_7b": cpu_int_mm_rate(reps, warmup)}
+    return res
 
 
 def run_reference(args):
@@ -209,16 +339,16 @@ def run_reference(args):
     if rank != 0:
         return  # the CPU reference runs once per node, on rank 0
     rows = int(os.environ.get("PN_REF_ROWS", "2048"))
-    rate, dt, kind, cores, desc = cpu_reference_rate(rows, max(1, args.steps), args.warmup)
-    line = {"metric": METRIC, "value": round(rate, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
+    res, _, _ = cpu_reference_rate(rows, max(1, args.steps), args.warmup)
+    rate = res["value"]
+    line = {"metric": METRIC, "value": rate, "unit": "GB/s", "n_gpus": args.gpus, "steps": res["reps"],
+            "warmup": args.warmup, "ms_per_step": round(res["s_per_sample"] * 1e3, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
             "config": {"workload": "70B-class decode GEMV: K->N 8192->28672 and 28672->8192, M in {1,8,64}",
-                       "sample": desc},
-            "cpu_baseline": {"value": round(rate, 3), "unit": "GB/s", "cores": cores, "kind": kind,
-                             "sample": desc},
-            "e2e": {"value": round(rate, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+                       "sample": res["sample"]},
+            "cpu_baseline": res,
+            "e2e": {"value": rate, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -251,26 +381,72 @@ def run_profile_case(args):
                       "launches": len(layers) * len(BATCHES)}))
 
 
-def prefill_int8(dev, gen, peaks):
+def _graph_time(fn, n_launch: int) -> float:
+    """Seconds per call of fn(i), i = 0..n_launch-1, from one CUDA graph replay."""
+    import torch
+    for i in range(2):
+        fn(i)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(n_launch):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) / n_launch * 1e-3
+
+
+def _max_over_ranks(v: float, world: int, dev) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def prefill_int8(dev, gen, peaks, world: int = 1, rank: int = 0):
     """Secondary measurement: the int8 prefill GEMM (per-token int8 activations
     x packed weights on the int8 tensor cores) at M = 4096 on the 7B-class
     layer shapes.  Reports the GEMM alone (activations already quantised) and
     with the activation quantiser, each from CUDA graphs of 12 launches that
     rotate over PREFILL_COPIES copies of weights and activations (more than L2
     between two uses of a copy).  Weights are in the layer's resident layout
-    (rows at a 16-byte stride, penta_kernel.pad_packed)."""
+    (rows at a 16-byte stride, penta_kernel.pad_packed).
+
+    At N > 1 every layer is column-sharded: rank r holds the packed rows
+    shard_range(N, r, world) (its output columns) and computes its (M, N/P)
+    block; the times are the max over ranks and the value counts the whole
+    layer's 2*M*N*K.  `with_all_gather` adds the NCCL all-gather of the output
+    blocks into the full (M, N) result (penta_dist.gather_columns, eager), and
+    the gathered result is compared bit for bit with the unsharded product."""
     import torch
     import penta_kernel as pk
+    import penta_dist as pd
     rows = []
-    tot_ops = tot_gemm = tot_e2e = 0.0
+    tot_ops = tot_gemm = tot_e2e = tot_gather = 0.0
     n_launch = 2 * PREFILL_COPIES
+    parity = True
     for (K, N) in PREFILL_SHAPES:
+        lo, hi = pd.shard_range(N, rank, world)
         packs, xs, xqs = [], [], []
-        for _ in range(PREFILL_COPIES):
+        full0 = None
+        for c in range(PREFILL_COPIES):
             w = torch.randn(N, K, device=dev, generator=gen) * 0.02
             packed, _, s = pk.quantize_and_pack(w)
             del w
-            packs.append((pk.pad_packed(packed), s))
+            if c == 0 and world > 1:
+                full0 = (pk.pad_packed(packed), s)
+            packs.append((pk.pad_packed(packed[lo:hi].contiguous()), s))
+            del packed
             x = torch.randn(PREFILL_M, K, device=dev, generator=gen).to(torch.bfloat16)
             xs.append(x)
             xqs.append(pk.quantize_activations_i8(x))
@@ -285,43 +461,60 @@ def prefill_int8(dev, gen, peaks):
             pw, s = packs[i % PREFILL_COPIES]
             return pk.penta_linear_i8(xs[i % PREFILL_COPIES], pw, s, K)
 
-        times = []
-        for fn in (gemm, full):
+        t_gemm = _max_over_ranks(_graph_time(gemm, n_launch), world, dev)
+        t_full = _max_over_ranks(_graph_time(full, n_launch), world, dev)
+        row = {"M": PREFILL_M, "K": K, "N": N, "cols_local": hi - lo, "gemm_us": round(t_gemm * 1e6, 1),
+               "with_quant_us": round(t_full * 1e6, 1)}
+        ops = 2.0 * PREFILL_M * N * K
+        if world > 1:
+            import torch.distributed as dist
+            y_full = torch.empty(PREFILL_M, N, dtype=torch.bfloat16, device=dev)
             for i in range(2):
-                fn(i)
+                pd.gather_columns(gemm(i), N, world, out=y_full)
             torch.cuda.synchronize()
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                for i in range(n_launch):
-                    fn(i)
-            g.replay()
-            torch.cuda.synchronize()
+            dist.barrier()
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
-            g.replay()
+            for i in range(n_launch):
+                pd.gather_columns(gemm(i), N, world, out=y_full)
             e1.record()
             torch.cuda.synchronize()
-            times.append(e0.elapsed_time(e1) / n_launch * 1e-3)
-            del g
-        ops = 2.0 * PREFILL_M * N * K
+            t_gather = _max_over_ranks(e0.elapsed_time(e1) / n_launch * 1e-3, world, dev)
+            row["with_all_gather_us"] = round(t_gather * 1e6, 1)
+            tot_gather += t_gather
+            # parity: the gathered columns equal the unsharded product bit for bit
+            pd.gather_columns(gemm(0), N, world, out=y_full)
+            xq, s_x, rowsum = xqs[0]
+            want = pk.penta_linear_i8_prequant(xq, s_x, rowsum, K, full0[0], full0[1])
+            ok = torch.tensor([1 if torch.equal(y_full, want) else 0], device=dev)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+            row["parity"] = "bit-exact" if int(ok.item()) == 1 else "MISMATCH"
+            parity = parity and int(ok.item()) == 1
+            del y_full, want
+        row["tops"] = round(ops / t_gemm / 1e12, 1)
         tot_ops += ops
-        tot_gemm += times[0]
-        tot_e2e += times[1]
-        rows.append({"M": PREFILL_M, "K": K, "N": N, "gemm_us": round(times[0] * 1e6, 1),
-                     "tops": round(ops / times[0] / 1e12, 1), "with_quant_us": round(times[1] * 1e6, 1)})
-        del packs, xs, xqs
+        tot_gemm += t_gemm
+        tot_e2e += t_full
+        rows.append(row)
+        del packs, xs, xqs, full0
         torch.cuda.empty_cache()
-    peak = 2.0 * peaks["bf16_tflops"]
-    return {"workload": f"int8 prefill GEMM, M={PREFILL_M}, K->N 4096->4096, 4096->11008, 11008->4096",
-            "inputs": f"{PREFILL_COPIES} copies of weights and activations rotated (larger than L2 between uses)",
-            "value": round(tot_ops / tot_gemm / 1e12, 1), "unit": "TOPS",
-            "with_activation_quant": round(tot_ops / tot_e2e / 1e12, 1),
-            "roofline": {"bound": "tensor", "achieved": round(tot_ops / tot_gemm / 1e12, 1), "peak": round(peak, 1),
-                         "unit": "TOP/s", "frac": round(tot_ops / tot_gemm / 1e12 / peak, 4),
-                         "peak_source": "2 x measured dense bf16 (MEASURED_PEAKS.json); B200's dense int8 rate "
-                                        "is twice its bf16 rate", "kernel": "pn::dqmm_kernel<I8, 256>"},
-            "per_shape": rows}
+    peak = 2.0 * peaks["bf16_tflops"] * world
+    res = {"workload": f"int8 prefill GEMM, M={PREFILL_M}, K->N 4096->4096, 4096->11008, 11008->4096"
+                       + (f", output columns sharded over {world} GPUs" if world > 1 else ""),
+           "inputs": f"{PREFILL_COPIES} copies of weights and activations rotated (larger than L2 between uses)",
+           "value": round(tot_ops / tot_gemm / 1e12, 1), "unit": "TOPS",
+           "with_activation_quant": round(tot_ops / tot_e2e / 1e12, 1),
+           "roofline": {"bound": "tensor", "achieved": round(tot_ops / tot_gemm / 1e12, 1), "peak": round(peak, 1),
+                        "unit": "TOP/s", "frac": round(tot_ops / tot_gemm / 1e12 / peak, 4),
+                        "peak_source": "2 x measured dense bf16 (MEASURED_PEAKS.json) per GPU x GPUs; B200's "
+                                       "dense int8 rate is twice its bf16 rate", "kernel": "pn::dqmm_kernel<I8, 256>"},
+           "per_shape": rows}
+    if world > 1:
+        res["with_all_gather"] = round(tot_ops / tot_gather / 1e12, 1)
+        res["per_gpu_tops"] = round(tot_ops / tot_gemm / 1e12 / world, 1)
+        res["parity"] = "bit-exact" if parity else "MISMATCH"
+    return res
 
 
 def pack_secondary(dev, peaks):
@@ -387,21 +580,30 @@ def pack_secondary(dev, peaks):
     return res
 
 
-def pentagpt_forward(dev):
+def pentagpt_forward(dev, world: int = 1, rank: int = 0):
     """Secondary measurement: PentaGPT-124M forward (prefill) tokens/s -- 12
     layers, d 768, every projection packed, batch 32 x 1024 random token ids,
     random weights from seed 42; last-position logits as the reference's
     inference forward.  bf16 projections (the parity path) and the per-token
-    int8 projections."""
+    int8 projections.  At N > 1 the batch is split over the ranks (pure
+    replicas, 32/N sequences each, no collective); the time is the max over
+    ranks and the value counts all 32 x 1024 tokens."""
     import torch
     from pentagpt import PentaGPTFast
     B, T = 32, 1024
-    idx = torch.randint(0, 50257, (B, T), generator=torch.Generator().manual_seed(42)).to(dev)
-    res = {"workload": "PentaGPT-124M forward, batch 32 x seq 1024, random init seed 42", "unit": "tokens/s"}
+    idx_all = torch.randint(0, 50257, (B, T), generator=torch.Generator().manual_seed(42))
+    per = B // world
+    idx = idx_all[rank * per:(rank + 1) * per].to(dev)
+    res = {"workload": "PentaGPT-124M forward, batch 32 x seq 1024, random init seed 42"
+                       + (f", batch split over {world} GPUs ({per} sequences each)" if world > 1 else ""),
+           "unit": "tokens/s"}
     for name, aq in (("bf16", None), ("int8", "int8")):
         model = PentaGPTFast.random(seed=42, device=dev, act_quant=aq)
         model(idx)
         torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         reps = 5
@@ -410,8 +612,8 @@ def pentagpt_forward(dev):
             model(idx)
         e1.record()
         torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / reps
-        res[name] = {"tokens_per_s": round(B * T / (ms * 1e-3)), "ms_per_forward": round(ms, 2)}
+        ms = _max_over_ranks(e0.elapsed_time(e1) / reps, world, dev)
+        res[name] = {"tokens_per_s": round(per * world * T / (ms * 1e-3)), "ms_per_forward": round(ms, 2)}
         del model
         torch.cuda.empty_cache()
     res["value"] = res["bf16"]["tokens_per_s"]
@@ -489,15 +691,19 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
     # ---- weights: quantise + pack each full layer on the GPU, keep this rank's rows
+    # (and, at N > 1, the whole packed layer for the parity check of the sharded outputs)
     gen = torch.Generator(device=dev).manual_seed(1234)
     packed = {}
     scales = {}
+    full = {}
     for (K, N) in SHAPES:
         w = torch.randn(N, K, device=dev, generator=gen) * 0.02
         p, _, s = pk.quantize_and_pack(w)
         del w
         lo, hi = pd.shard_range(N, rank, world)
         base = p[lo:hi].contiguous()
+        if world > 1:
+            full[(K, N)] = p
         del p
         packed[(K, N)] = [base] + [base.clone() for _ in range(COPIES - 1)]
         scales[(K, N)] = s
@@ -506,26 +712,26 @@ def run_ours(args):
 
     seq = launches_per_step()
     # N > 1: each product's GEMM stores its output columns into every GPU's
-    # full-output buffer (peer memory), then a cross-GPU barrier kernel.
+    # full-output buffer (peer memory), then a cross-GPU barrier kernel.  Four
+    # buffer sets: the end-to-end graph gives each of its four steps its own.
     peers = pd.PeerGroup() if world > 1 else None
-    outs_peer = [peers.buffer((M, N), torch.bfloat16) for (M, K, N) in seq] if peers else None
+    outs_sets = [[peers.buffer((M, N), torch.bfloat16) for (M, K, N) in seq] for _ in range(4)] if peers else None
     col0 = {(K, N): pd.shard_range(N, rank, world)[0] for (K, N) in SHAPES}
 
-    def product(l: int, c: int, barrier: bool = True):
+    def product(l: int, c: int, barrier: bool = True, x=None, bufset: int = 0):
         M, K, N = seq[l]
+        xin = xs[(M, K)] if x is None else x
         if peers is None:
-            return pk.penta_linear(xs[(M, K)], packed[(K, N)][c], scales[(K, N)], K)
-        pd.linear_peers(xs[(M, K)], packed[(K, N)][c], scales[(K, N)], K, col0[(K, N)], outs_peer[l][1], N)
+            return pk.penta_linear(xin, packed[(K, N)][c], scales[(K, N)], K)
+        out = outs_sets[bufset][l]
+        pd.linear_peers(xin, packed[(K, N)][c], scales[(K, N)], K, col0[(K, N)], out[1], N)
         if barrier:
             peers.barrier()
-        return outs_peer[l][0]
+        return out[0]
 
-    def run_step(i: int, outs=None):
+    def run_step(i: int):
         for l, (M, K, N) in enumerate(seq):
-            c = ((6 * i + l) // 2) % COPIES
-            y = product(l, c)
-            if outs is not None:
-                outs.append(y)
+            product(l, ((6 * i + l) // 2) % COPIES)
 
     for i in range(3):
         run_step(i)
@@ -534,46 +740,40 @@ def run_ours(args):
     # One CUDA graph per step phase removes host launch cost (at N > 1 the
     # graphs hold the GEMMs and the cross-GPU barrier kernels, no NCCL calls).
     graphs = []
-    if True:
-        for ph in range(4):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                run_step(ph)
-            graphs.append(g)
-        torch.cuda.synchronize()
+    for ph in range(4):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            run_step(ph)
+        graphs.append(g)
+    torch.cuda.synchronize()
 
     def step(i):
-        if graphs:
-            graphs[i % 4].replay()
-        else:
-            run_step(i)
+        graphs[i % 4].replay()
 
-    for i in range(args.warmup):
-        step(i)
     sampler = ClockSampler([local] if world == 1 else list(range(torch.cuda.device_count()))[:world]) \
         if rank == 0 else None
+    if sampler:
+        sampler.start()
+    for i in range(args.warmup):
+        step(i)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    if sampler:
-        sampler.start()
     stream = torch.cuda.current_stream()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    h0 = time.time()
     t0.record(stream)
     for i in range(args.steps):
         step(i)
     t1.record(stream)
     torch.cuda.synchronize()
+    h1 = time.time()
+    if sampler:
+        sampler.window = (h0, h1)
     if world > 1:
         dist.barrier()
-    if sampler:
-        sampler.stop()
-    ms = t0.elapsed_time(t1)
-    if world > 1:
-        tt = torch.tensor([ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
+    ms = _max_over_ranks(t0.elapsed_time(t1), world, dev)
     ms_per_step = ms / args.steps
     value = step_bytes() * args.steps / (ms * 1e-3) / 1e9
 
@@ -602,55 +802,74 @@ def run_ours(args):
         b = alg_bytes(M, K, n_loc)
         per.append({"M": M, "K": K, "N": N, "rows_local": n_loc, "us": round(dur * 1e3, 2),
                     "gbs": round(b / (dur * 1e-3) / 1e9, 1)})
+    if sampler:
+        sampler.stop()
     peaks = measured_peaks()
     tot_b = sum(alg_bytes(p["M"], p["K"], p["rows_local"]) for p in per)
     tot_t = sum(p["us"] for p in per) * 1e-6
     achieved = tot_b / tot_t / 1e9
-    traffic = profile_traffic()
+    traffic, traffic_src = profile_traffic()
 
-    # ---- end to end through the public API with host buffers (pinned), eager calls.
-    # Single GPU: host -> device copies on one stream, the products
-    # (penta_linear) on the compute stream, device -> host copies on a third,
-    # joined per product by events, so the two copy engines and the SMs work
-    # on different products at once (as a serving loop overlaps them); every
-    # step moves all its inputs and outputs.
+    # ---- parity of the timed path: every product as the step runs it, against
+    # the unsharded product of the whole layer (N > 1: on every rank, the full
+    # output assembled by the peer stores; sharding changes the k split of the
+    # tiles, hence the fp32 summation order: within one bf16 ulp)
+    parity = check_parity(pk, seq, product, xs, packed, full, scales, world, dev)
+
+    # ---- end to end through the public API with host buffers (pinned).
+    # Host -> device copies on one stream, the products on the compute stream
+    # (penta_linear; at N > 1 penta_dist.linear_peers + the cross-GPU barrier),
+    # device -> host copies on a third, joined per product by events, so the
+    # copy engines and the SMs work on different products at once (as a
+    # serving loop overlaps them); every step moves all its inputs and outputs.
+    # At N > 1 the products write fixed peer buffers, so each step has its own
+    # buffer set and the compute stream waits for the step's device -> host
+    # copies before the next step's first barrier (no rank overwrites a buffer
+    # that another rank is still copying out).
     xh = {k: v.cpu().pin_memory() for k, v in xs.items()}
     yh = {(M, K, N): torch.empty(M, N, dtype=torch.bfloat16).pin_memory() for (M, K, N) in seq}
-    xd = {k: torch.empty_like(v) for k, v in xs.items()}
     h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     xd_l = [torch.empty(M, K, dtype=torch.bfloat16, device=dev) for (M, K, N) in seq]
     ev_in = [torch.cuda.Event() for _ in seq]    # x of product l on the device
     ev_out = [torch.cuda.Event() for _ in seq]   # product l done (its x buffer free, its y ready)
 
-    def e2e_step(i):
-        if peers is not None:
-            for l, (M, K, N) in enumerate(seq):
-                c = ((6 * i + l) // 2) % COPIES
-                xd[(M, K)].copy_(xh[(M, K)], non_blocking=True)
-                pd.linear_peers(xd[(M, K)], packed[(K, N)][c], scales[(K, N)], K, col0[(K, N)], outs_peer[l][1], N)
-                peers.barrier()
-                yh[(M, K, N)].copy_(outs_peer[l][0], non_blocking=True)
-            return
+    def e2e_step(i, first=False, capturing=False):
+        cs = torch.cuda.current_stream()
         with torch.cuda.stream(h2d_s):
             for l, (M, K, N) in enumerate(seq):
-                h2d_s.wait_event(ev_out[l])  # the previous step's product l has read xd_l[l]
+                if not first:
+                    h2d_s.wait_event(ev_out[l])  # the previous step's product l has read xd_l[l]
                 xd_l[l].copy_(xh[(M, K)], non_blocking=True)
                 ev_in[l].record(h2d_s)
         ys = []
         for l, (M, K, N) in enumerate(seq):
-            c = ((6 * i + l) // 2) % COPIES
-            stream.wait_event(ev_in[l])
-            ys.append(pk.penta_linear(xd_l[l], packed[(K, N)][c], scales[(K, N)], K))
-            ev_out[l].record(stream)
+            cs.wait_event(ev_in[l])
+            ys.append(product(l, ((6 * i + l) // 2) % COPIES, x=xd_l[l], bufset=i % 4))
+            ev_out[l].record(cs)
         with torch.cuda.stream(d2h_s):
             for l, (M, K, N) in enumerate(seq):
                 d2h_s.wait_event(ev_out[l])
                 yh[(M, K, N)].copy_(ys[l], non_blocking=True)
-                ys[l].record_stream(d2h_s)
+                if peers is None and not capturing:
+                    ys[l].record_stream(d2h_s)
+        if peers is not None:
+            cs.wait_stream(d2h_s)
+
+    def check_host_outputs(i):
+        bad = 0
+        for l, (M, K, N) in enumerate(seq):
+            c = ((6 * i + l) // 2) % COPIES
+            if peers is None:
+                want = pk.penta_linear(xd_l[l], packed[(K, N)][c], scales[(K, N)], K).cpu()
+                bad += 0 if torch.equal(yh[(M, K, N)], want) else 1
+            else:  # copies hold the same rows; the whole layer's product, one bf16 ulp
+                want = pk.penta_linear(xd_l[l], full[(K, N)], scales[(K, N)], K).cpu()
+                bad += 0 if within_bf16_ulp(yh[(M, K, N)], want) else 1
+        return bad
 
     e2e_steps = max(1, min(args.steps, 200))
     for i in range(3):
-        e2e_step(i)
+        e2e_step(i, first=(i == 0))
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -665,17 +884,8 @@ def run_ours(args):
     stream.wait_stream(d2h_s)
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        tt = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_ms = float(tt.item())
-    if peers is None:
-        # the host outputs of the last step are the products of that step's weight copies
-        for l, (M, K, N) in enumerate(seq):
-            c = ((6 * (e2e_steps - 1) + l) // 2) % COPIES
-            want = pk.penta_linear(xd_l[l], packed[(K, N)][c], scales[(K, N)], K).cpu()
-            assert torch.equal(yh[(M, K, N)], want), f"e2e output of product {l} differs"
+    e2e_ms = _max_over_ranks(e0.elapsed_time(e1), world, dev)
+    bad = check_host_outputs(e2e_steps - 1)
     e2e_eager = step_bytes() * e2e_steps / (e2e_ms * 1e-3) / 1e9
     h2d = sum(2 * M * K for (M, K, N) in seq)
     d2h = sum(2 * M * N for (M, K, N) in seq)
@@ -684,62 +894,53 @@ def run_ours(args):
     # so the weight-copy rotation is kept) and replayed: what a serving loop
     # that graphs its decode step gets, without the eager loop's host time.
     # Every replayed step still copies all inputs in and all outputs out.
-    e2e_graph = None
-    if peers is None:
-        cap = torch.cuda.Stream(dev)
-        cap.wait_stream(stream)
-        g_e2e = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_e2e, stream=cap):
-            h2d_s.wait_stream(cap)
-            d2h_s.wait_stream(cap)
-            for i in range(4):
-                with torch.cuda.stream(h2d_s):
-                    for l, (M, K, N) in enumerate(seq):
-                        if i > 0:
-                            h2d_s.wait_event(ev_out[l])
-                        xd_l[l].copy_(xh[(M, K)], non_blocking=True)
-                        ev_in[l].record(h2d_s)
-                ys = []
-                for l, (M, K, N) in enumerate(seq):
-                    c = ((6 * i + l) // 2) % COPIES
-                    cap.wait_event(ev_in[l])
-                    ys.append(pk.penta_linear(xd_l[l], packed[(K, N)][c], scales[(K, N)], K))
-                    ev_out[l].record(cap)
-                with torch.cuda.stream(d2h_s):
-                    for l, (M, K, N) in enumerate(seq):
-                        d2h_s.wait_event(ev_out[l])
-                        yh[(M, K, N)].copy_(ys[l], non_blocking=True)
-            cap.wait_stream(h2d_s)
-            cap.wait_stream(d2h_s)
-        reps = max(1, e2e_steps // 4)
-        for _ in range(2):
-            g_e2e.replay()
-        torch.cuda.synchronize()
-        e0.record(stream)
-        for _ in range(reps):
-            g_e2e.replay()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        e2e_graph = step_bytes() * 4 * reps / (e0.elapsed_time(e1) * 1e-3) / 1e9
-        for l, (M, K, N) in enumerate(seq):
-            c = ((6 * 3 + l) // 2) % COPIES
-            want = pk.penta_linear(xd_l[l], packed[(K, N)][c], scales[(K, N)], K).cpu()
-            assert torch.equal(yh[(M, K, N)], want), f"graphed e2e output of product {l} differs"
-        del g_e2e
-    e2e_val = e2e_graph if e2e_graph is not None else e2e_eager
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    g_e2e = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_e2e, stream=cap):
+        h2d_s.wait_stream(cap)
+        d2h_s.wait_stream(cap)
+        for i in range(4):
+            e2e_step(i, first=(i == 0), capturing=True)
+        cap.wait_stream(h2d_s)
+        cap.wait_stream(d2h_s)
+    reps = max(1, e2e_steps // 4)
+    for _ in range(2):
+        g_e2e.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0.record(stream)
+    for _ in range(reps):
+        g_e2e.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_graph = step_bytes() * 4 * reps / (_max_over_ranks(e0.elapsed_time(e1), world, dev) * 1e-3) / 1e9
+    bad += check_host_outputs(3)
+    del g_e2e
+    if world > 1:
+        t = torch.tensor([bad], device=dev)
+        dist.all_reduce(t)
+        bad = int(t.item())
+    if bad:
+        raise SystemExit(f"end-to-end host outputs differ from the product in {bad} cases")
+    e2e_val = e2e_graph
 
-    prefill = None
-    gpt = None
-    packsec = None
-    if world == 1 and not args.no_prefill:
-        prefill = prefill_int8(dev, gen, peaks)
-        gpt = pentagpt_forward(dev)
-        packsec = pack_secondary(dev, peaks)
+    prefill = gpt = packsec = None
+    if not args.no_prefill:
+        prefill = prefill_int8(dev, gen, peaks, world, rank)
+        gpt = pentagpt_forward(dev, world, rank)
+        if world == 1:
+            packsec = pack_secondary(dev, peaks)
+    if prefill is not None and prefill.get("parity", "bit-exact") != "bit-exact":
+        raise SystemExit("sharded int8 prefill output differs from the unsharded product")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        rate, dt, kind, cores, desc = cpu_reference_rate(int(os.environ.get("PN_REF_ROWS", "2048")), 2, 1)
-        cpu = {"value": round(rate, 3), "unit": "GB/s", "cores": cores, "kind": kind, "sample": desc}
+        cpu = cpu_legs(max(1, args.steps), args.warmup)
 
     if rank == 0:
         line = {
@@ -755,18 +956,21 @@ def run_ours(args):
                        f"output rows sharded x{world}; outputs stored into every GPU's buffer by the GEMM "
                        f"(NVLink peer stores) + cross-GPU barrier kernel",
                        "timing": "CUDA graphs of one step"},
+            "parity": parity,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                         "traffic_source": traffic_src,
                          "peak_source": peaks["source"], "kernel": "pn::dqmm_kernel<F16, BT>",
                          "per_launch": per},
             "e2e": {"value": round(e2e_val, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps, "eager_value": round(e2e_eager, 1),
-                    "graphed": e2e_graph is not None,
-                    "path": ("penta_kernel.penta_linear on the compute stream, pinned host->device and "
-                             "device->host copies of every product's x and y on two other streams, joined per "
-                             "product by events; value: those calls captured in a CUDA graph of four steps and "
-                             "replayed, eager_value: the eager loop" if world == 1 else
-                             "penta_dist.linear_peers + barrier, pinned host x/y copies per call, eager")},
+                    "graphed": True,
+                    "path": ("penta_kernel.penta_linear" if world == 1 else
+                             "penta_dist.linear_peers + PeerGroup.barrier (outputs in every GPU's buffer)")
+                            + " on the compute stream, pinned host->device and device->host copies of every "
+                              "product's x and y on two other streams, joined per product by events; value: "
+                              "those calls captured in a CUDA graph of four steps and replayed, eager_value: "
+                              "the eager loop; the host outputs of the last step of each are checked"},
             "cpu_baseline": cpu,
             # per product: the activation re-layout kernel and the dqmm kernel
             # (+ the cross-GPU barrier kernel when sharded)
@@ -782,6 +986,42 @@ def run_ours(args):
         dist.barrier()
         peers.close()
         dist.destroy_process_group()
+
+
+def within_bf16_ulp(y, want) -> bool:
+    """|y - want| <= one bf16 ulp of want (+1e-6) elementwise (both bf16 tensors)."""
+    import torch
+    a = y.float().double()
+    b = want.float().double()
+    ulp = torch.ldexp(torch.ones_like(b), (torch.frexp(b.abs().clamp(min=1e-30))[1] - 8))
+    return bool(((a - b).abs() <= ulp + 1e-6).all())
+
+
+def check_parity(pk, seq, product, xs, packed, full, scales, world, dev) -> str:
+    """At N > 1: runs every product of the step once more as the timed path
+    runs it (sharded GEMM, peer stores, barrier) and compares the full output
+    on every rank with the unsharded product of the whole layer; exits non-zero
+    on a mismatch."""
+    import torch
+    if world == 1:
+        return "n/a at N = 1: the unsharded path (tests/test_linear_gpu.py checks it against the oracle)"
+    bad = []
+    for l, (M, K, N) in enumerate(seq):
+        y = product(l, 0).clone()
+        torch.cuda.synchronize()
+        ok = within_bf16_ulp(y, pk.penta_linear(xs[(M, K)], full[(K, N)], scales[(K, N)], K))
+        if not ok:
+            bad.append(l)
+    n_bad = len(bad)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([n_bad], device=dev)
+        dist.all_reduce(t)
+        n_bad = int(t.item())
+    if n_bad:
+        raise SystemExit(f"sharded output parity failed: {n_bad} (product, rank) cases, here {bad}")
+    return (f"ok: on all {world} ranks the full output of each of the six products, assembled by the "
+            f"peer stores, is within one bf16 ulp of the unsharded product")
 
 
 def main():

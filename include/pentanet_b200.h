@@ -237,6 +237,15 @@ int pn_linear_bf16_peers(const void *x, int64_t M, int64_t K, const int32_t *pac
  * bounded (PN_ERR_TIMEOUT in the device status word). */
 int pn_peer_barrier(int *const *flags, int world, int rank, int *gen, void *stream);
 
+/* pn_peer_barrier with an explicit wait limit: each rank's wait ends after
+ * wait_ns nanoseconds (0 = the default of 2 s) with PN_ERR_TIMEOUT recorded
+ * in the device status word, and the kernel returns.  After a timeout the
+ * generations are out of step: with no barrier in flight on any rank, every
+ * rank zeroes its flag array and gen before the next barrier
+ * (penta_dist.PeerGroup.reset).  No counterpart in the reference, which has
+ * no multi-GPU code. */
+int pn_peer_barrier_wait(int *const *flags, int world, int rank, int *gen, int64_t wait_ns, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -223,6 +223,18 @@ def ref_avx2() -> ctypes.CDLL:
     return _ref
 
 
+def ref_omp_threads(n: int | None = None) -> int:
+    """Set (when n is given) and return the OpenMP thread count the reference's
+    kernel runs with on the calling thread.  Launchers such as torchrun export
+    OMP_NUM_THREADS=1, which libgomp reads once at start-up; the timed CPU
+    baseline sets the count explicitly instead of inheriting that."""
+    ref_avx2()  # loads the libgomp the kernel is linked against
+    gomp = ctypes.CDLL("libgomp.so.1")
+    if n is not None:
+        gomp.omp_set_num_threads(ctypes.c_int(int(n)))
+    return int(gomp.omp_get_max_threads())
+
+
 def ref_avx2_unpack(packed: np.ndarray, K: int) -> np.ndarray:
     """penta_unpack (penta_avx2_wrapper.py:37-53) via the reference C kernel."""
     packed = np.ascontiguousarray(packed, dtype=np.int32)

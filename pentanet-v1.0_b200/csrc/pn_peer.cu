@@ -16,13 +16,23 @@ namespace pn {
 // rank's flag array (system-scope release), then waits until every slot of
 // its own array holds at least that generation (system-scope acquire).  The
 // generation counter lives in device memory, so a captured CUDA graph replays
-// correctly.  Waits are bounded: on timeout the device status word records
-// PN_ERR_TIMEOUT and the kernel returns.
+// correctly.  Waits are bounded (wait_ns of the global nanosecond timer): on
+// timeout the device status word records PN_ERR_TIMEOUT and the kernel
+// returns.  After a timeout the ranks' generations are out of step; every
+// rank must then re-zero its flag array and generation (with no barrier in
+// flight anywhere) before the next barrier.
 struct PeerFlags {
     int* flags[8];  // flags[r] = rank r's array of `world` ints (peer pointers)
 };
 
-__global__ void __launch_bounds__(32) peer_barrier_kernel(PeerFlags f, int world, int rank, int* gen) {
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__global__ void __launch_bounds__(32) peer_barrier_kernel(PeerFlags f, int world, int rank, int* gen,
+                                                          uint64_t wait_ns) {
     // The next product's pre-pass (a programmatic dependent) may be scheduled
     // during the exchange: it waits for this grid's completion before it
     // touches memory, and the GEMM after it starts streaming weights.
@@ -42,12 +52,12 @@ __global__ void __launch_bounds__(32) peer_barrier_kernel(PeerFlags f, int world
     }
     if (lane < world) {
         const int* mine = f.flags[rank] + lane;
-        const long long t0 = clock64();
+        const uint64_t t0 = global_ns();
         while (true) {
             int v;
             asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
             if (v - g >= 0) break;
-            if (clock64() - t0 > (1ll << 31)) {
+            if (global_ns() - t0 > wait_ns) {
                 record_status(PN_ERR_TIMEOUT);
                 break;
             }
@@ -60,6 +70,11 @@ __global__ void __launch_bounds__(32) peer_barrier_kernel(PeerFlags f, int world
 }  // namespace pn
 
 namespace {
+// Default wait of the cross-GPU barrier: long enough for any product the
+// ranks run between two barriers, short enough that a missing rank surfaces
+// as PN_ERR_TIMEOUT within seconds.
+constexpr uint64_t kPeerWaitDefaultNs = 2000000000ull;
+
 typedef CUresult (*GetAddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
 GetAddressRangeFn address_range_fn() {
     static GetAddressRangeFn fn = [] {
@@ -107,6 +122,13 @@ extern "C" int pn_ipc_close(void* ptr) {
 }
 
 extern "C" int pn_peer_barrier(int* const* flags, int world, int rank, int* gen, void* stream) {
+    return pn_peer_barrier_wait(flags, world, rank, gen, 0, stream);
+}
+
+extern "C" int pn_peer_barrier_wait(int* const* flags, int world, int rank, int* gen, int64_t wait_ns,
+                                    void* stream) {
+    if (wait_ns < 0) return fail(PN_ERR_ARG, "pn_peer_barrier_wait: wait_ns=%lld", (long long)wait_ns);
+    const uint64_t limit = wait_ns == 0 ? kPeerWaitDefaultNs : (uint64_t)wait_ns;
     if (world < 1 || world > 8 || rank < 0 || rank >= world || !flags || !gen)
         return fail(PN_ERR_ARG, "pn_peer_barrier: world=%d rank=%d", world, rank);
     pn::PeerFlags f{};
@@ -115,7 +137,7 @@ extern "C" int pn_peer_barrier(int* const* flags, int world, int rank, int* gen,
         f.flags[r] = flags[r];
     }
     if (int st = check_device()) return st;
-    pn::peer_barrier_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(f, world, rank, gen);
+    pn::peer_barrier_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(f, world, rank, gen, limit);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? ok() : cuda_fail(e, "pn_peer_barrier");
 }

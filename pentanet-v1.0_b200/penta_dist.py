@@ -359,11 +359,30 @@ class PeerGroup:
         self._keep.append(t)
         return t, self._exchange(t)
 
-    def barrier(self, stream=None) -> None:
+    def barrier(self, stream=None, wait_ns: int = 0) -> None:
+        """Enqueue the cross-GPU barrier.  Each rank's wait is bounded (wait_ns
+        nanoseconds, 0 = the library default of 2 s); a wait that runs out
+        leaves PN_ERR_TIMEOUT in the device status word
+        (penta_native.device_status) and the group needs reset()."""
         s = stream if stream is not None else torch.cuda.current_stream()
         arr = (ctypes.c_void_p * self.world)(*self._flag_ptrs)
-        nat.check(self._lib.pn_peer_barrier(arr, self.world, self.rank, self.gen.data_ptr(), s.cuda_stream),
-                  "pn_peer_barrier")
+        nat.check(self._lib.pn_peer_barrier_wait(arr, self.world, self.rank, self.gen.data_ptr(), int(wait_ns),
+                                                 s.cuda_stream), "pn_peer_barrier_wait")
+
+    def reset(self) -> None:
+        """Bring the barrier back into step after a wait ran out: every rank
+        calls it (a host collective).  Each rank first lets its own kernels
+        finish (every wait is bounded), the process group's barrier then
+        guarantees that no barrier kernel is in flight on any rank, and only
+        then does each rank zero its flag array and generation counter; a
+        second host barrier keeps any rank from starting a new device
+        barrier before all have zeroed."""
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        self.flags.zero_()
+        self.gen.zero_()
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
 
     def close(self) -> None:
         torch.cuda.synchronize()

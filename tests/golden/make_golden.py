@@ -2,7 +2,9 @@
 
 Run from the repository root on a machine where the reference tree is mounted:
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <reference checkout>
+
+(or set PENTANET_REF_DIR to the checkout instead of passing --ref).
 
 It imports the reference's own modules -- ``penta_kernel`` (quantize_and_pack,
 unpack_weights, memory_stats; penta_kernel.py:42-106) and ``penta_kernel_cpu``
@@ -65,8 +67,11 @@ def tie_weight(N: int, K: int) -> torch.Tensor:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("PENTANET_REF_DIR"),
+                    help="the reference checkout (default: $PENTANET_REF_DIR)")
     args = ap.parse_args()
+    if not args.ref or not os.path.isfile(os.path.join(args.ref, "penta_kernel.py")):
+        ap.error("pass --ref <reference checkout> (or set PENTANET_REF_DIR)")
     sys.path.insert(0, args.ref)
     sys.path.insert(0, ROOT)
     import penta_kernel as pk          # reference module

@@ -1,6 +1,8 @@
 """Per-token int8 activation quantiser and the int8 tensor-core GEMM against the
 oracle: xq, s_x and int32 accumulators bit-exact (= torch._int_mm), outputs
 exact to the reference's epilogue formula (penta_avx2_wrapper.py:147)."""
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -69,8 +71,12 @@ def test_int8_bias_and_zero_rows(cuda_device):
 
 @pytest.mark.parametrize("K,N", [(4096, 4096), (4096, 11008), (11008, 4096)])
 def test_cfg3_full_size(cuda_device, K, N):
-    """7B-class prefill shapes at M=4096: exact int32 checksum of checksums
-    (sum_n acc[m, n] = xq[m] . colsum(w)) and exact oracle rows/columns."""
+    """7B-class prefill shapes at M=4096: every int32 accumulator equal to the
+    exact integer product (CPU torch._int_mm of the same int8 activations and
+    unpacked weights, in row blocks; the int8 line's own arithmetic,
+    penta_avx2_wrapper.py:130-131,147), the exact checksum of checksums
+    (sum_n acc[m, n] = xq[m] . colsum(w)), and sampled outputs against the
+    oracle's epilogue."""
     M = 4096
     packed, _, gamma = pk.quantize_and_pack(gen_weight(N, K, seed=K * 7 + N).to(cuda_device))
     x = gen_act(M, K, seed=N).to(torch.bfloat16).to(cuda_device)
@@ -78,18 +84,20 @@ def test_cfg3_full_size(cuda_device, K, N):
     y, acc = pk.penta_linear_i8_prequant(xq, s_x, rowsum, K, packed, gamma, out_dtype=torch.float32,
                                          return_acc=True)
     w8 = pk.unpack_weights_i8(packed, K)
+    acc_c = acc.cpu()
+    xq_c = xq[:, :K].cpu()
+    wt_c = w8.cpu().t().contiguous()
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    for r0 in range(0, M, 1024):
+        want = torch._int_mm(xq_c[r0:r0 + 1024].contiguous(), wt_c)
+        assert torch.equal(acc_c[r0:r0 + 1024], want), f"int32 accumulators differ in rows {r0}..{r0 + 1023}"
     # float64 sums of these integers are exact (all partial sums < 2^53)
     xqd = xq[:, :K].double()
     w8d = w8.double()
     assert torch.equal(acc.double().sum(1), xqd @ w8d.sum(0))
-    assert torch.equal(acc.double().sum(0), xqd.sum(0) @ w8d.T)
     rows = torch.tensor([0, 1, 2047, M - 1])
-    cols = torch.tensor([0, 5, N // 3, N - 1])
-    xq_np = xq[rows, :K].cpu().numpy()
-    want = orc.matmul_i8(xq_np, w8.cpu().numpy())
+    want = orc.matmul_i8(xq[rows, :K].cpu().numpy(), w8.cpu().numpy())
     assert np.array_equal(acc[rows].cpu().numpy(), want)
-    want_c = orc.matmul_i8(xq[:, :K].cpu().numpy(), w8[cols].cpu().numpy())
-    assert np.array_equal(acc[:, cols].cpu().numpy(), want_c)
     assert np.array_equal(y[rows].cpu().numpy(), orc.dequant_i8(want, s_x[rows].cpu().numpy(), gamma))
 
 

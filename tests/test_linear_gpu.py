@@ -124,27 +124,29 @@ def test_errors_like_reference(cuda_device):
         pk.penta_linear(torch.zeros(2, 30, dtype=torch.bfloat16, device=cuda_device), packed, gamma, 40)
 
 
-def test_cfg4_full_size_properties(cuda_device):
-    """70B-class decode shapes at full size: linearity and a checksum-of-
-    checksums against the oracle (sum over n of y[m, n] = x[m] . colsum(w)),
-    plus exact oracle rows for a sample of outputs."""
-    for (K, N) in [(8192, 28672), (28672, 8192)]:
-        packed, gamma, _ = _layer(N, K, seed=K + N, dev=cuda_device)
-        M = 8
-        x = gen_act(M, K, seed=K).to(torch.bfloat16).to(cuda_device)
-        y = pk.penta_linear(x, packed, gamma, K, out_dtype=torch.float32).double()
-        # linearity: y(2x) = 2 y(x) exactly (power-of-two scaling)
+@pytest.mark.parametrize("K,N", [(8192, 28672), (28672, 8192)])
+def test_cfg4_full_size(cuda_device, K, N):
+    """70B-class decode shapes at full size, M = 1, 8, 64: every output (fp32
+    and bf16) against the oracle's float64 product of the unpacked weights,
+    plus two size-independent properties: exact linearity under x -> 2x and a
+    checksum of checksums (sum over n of y[m, n] = x[m] . colsum(w))."""
+    packed, gamma, _ = _layer(N, K, seed=K + N, dev=cuda_device)
+    w8 = pk.unpack_weights_i8(packed, K)
+    w8_np = w8.cpu().numpy()
+    colsum = w8.to(torch.float64).sum(0)
+    for M in (1, 8, 64):
+        x = gen_act(M, K, seed=K + M).to(torch.bfloat16).to(cuda_device)
+        want = orc.matmul_f64(x.float().cpu().numpy(), w8_np, gamma)
+        y = pk.penta_linear(x, packed, gamma, K, out_dtype=torch.float32)
+        assert_close(y.cpu().numpy(), want, what=f"cfg4 {K}->{N} M={M} fp32")
+        yb = pk.penta_linear(x, packed, gamma, K)
+        assert_bf16_close(yb.float().cpu().numpy(), want, what=f"cfg4 {K}->{N} M={M} bf16")
+        yd = y.double()
         y2 = pk.penta_linear(x * 2, packed, gamma, K, out_dtype=torch.float32).double()
-        assert torch.equal(y2, 2 * y)
-        # checksum of checksums via the unpacked column sums
-        w8 = pk.unpack_weights_i8(packed, K)
-        colsum = w8.to(torch.float64).sum(0)
-        want = (x.double() @ colsum) * gamma
-        got = y.sum(1)
-        assert torch.allclose(got, want, rtol=1e-6, atol=1e-3 * N ** 0.5)
-        rows = torch.tensor([0, 1, N // 2, N - 1])
-        sample = orc.matmul_f64(x.float().cpu().numpy(), w8[rows].cpu().numpy(), gamma)
-        assert_close(y[:, rows].cpu().numpy(), sample, what=f"cfg4 {K}->{N} sample")
+        assert torch.equal(y2, 2 * yd)
+        got = yd.sum(1)
+        ref = (x.double() @ colsum) * gamma
+        assert torch.allclose(got, ref, rtol=1e-6, atol=1e-3 * N ** 0.5)
 
 
 def test_no_device_timeouts(cuda_device):

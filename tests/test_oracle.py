@@ -161,3 +161,22 @@ def test_ternary_rule():
     want = np.clip(np.rint(w.astype(np.float32) / np.float32(gamma)), -1, 1).astype(np.int8)
     assert np.array_equal(q, want)
     assert list(q[0, :4]) == [0, 0, 1, -1]
+
+
+@pytest.mark.parametrize("name", ["cfg0"] + [n for n in META["cases"] if n.startswith("small.")][:4])
+def test_numba_port_matches_reference_numba(name):
+    """oracle/numba_port.py (the timed numba CPU leg) against the reference's own
+    numba penta_linear_cpu outputs stored in the fixtures."""
+    import torch
+    from oracle import numba_port as nbp
+    if not nbp.AVAILABLE:
+        pytest.skip("numba not importable")
+    c = META["cases"][name]
+    if name == "cfg0":
+        w, x = gen_weight(3072, 768, seed=0), gen_act(8, 768, seed=100)
+    else:
+        w = gen_weight(c["N"], c["K"], seed=c["w_seed"], std=c["std"])
+        x = gen_act(3, c["K"], seed=c["x_seed"])
+    packed, _, gamma = orc.quantize_pack(w.numpy())
+    y = nbp.penta_linear_cpu(x, torch.from_numpy(packed), gamma, c["K"]).numpy()
+    assert np.abs(y - G[f"{name}.y_numba"]).max() < 1e-5
