@@ -60,7 +60,15 @@ size_t pn_absmean_workspace_size(void);
 /* gamma = max(mean|W|, 1e-8) as a float written to d_scale (device pointer):
  * penta_kernel.py:57.  W has n_elems elements of w_dtype (PN_F32 or PN_BF16).
  * The sum of |W| is accumulated in double in a fixed order, so the result is
- * deterministic. */
+ * deterministic.
+ * Stated deviation: gamma is the correctly rounded mean (double sum, one
+ * rounding to float).  The reference's torch fp32 CPU mean is not always
+ * correctly rounded; in 10 of the 17 reference fixtures the two differ by one
+ * float ulp.  The packed bytes were identical in every fixture.  A W/gamma
+ * quotient lying within about one ulp of a half-integer could round the
+ * other way under the reference's gamma.  Callers that must reproduce the
+ * reference's gamma exactly pass their own scale to pn_quantize_pack
+ * (quantize_and_pack(w, scale=...)). */
 int pn_absmean_scale(const void *w, int w_dtype, int64_t n_elems, float *d_scale, void *workspace,
                      size_t workspace_bytes, void *stream);
 
@@ -86,6 +94,15 @@ int pn_unpack(const int32_t *packed, int64_t N, int64_t K_packs, int64_t K_orig,
 
 /* ---- fused dequant-matmul: replaces penta_linear / _penta_matmul_kernel
  *      (penta_kernel.py:111-278) ------------------------------------------- */
+
+/* bf16 products of at most this many tokens (0..8; default 0) whose packed
+ * rows sit at a 16-byte pitch run on the CUDA-core decode GEMV (fp32 FMAs of
+ * the masked codes, no tensor cores); larger ones on the tensor-core kernel.
+ * Both compute the same fp32-accumulated product (results may differ in the
+ * last bf16 bit, the summation order being different).  Sets the limit when
+ * max_tokens >= 0 and returns the previous one.  Process-wide.  No
+ * counterpart in the reference. */
+int pn_set_gemv_max_tokens(int max_tokens);
 
 /* Recommended workspace bytes for pn_linear_bf16 / pn_linear_i8 at this shape
  * (0 allowed when the result is 0).  kind: PN_BF16 or PN_I8.  With this much

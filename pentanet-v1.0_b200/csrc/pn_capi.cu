@@ -164,6 +164,12 @@ int pn_unpack(const int32_t* packed, int64_t N, int64_t K_packs, int64_t K_orig,
     return e == cudaSuccess ? ok() : cuda_fail(e, "pn_unpack");
 }
 
+int pn_set_gemv_max_tokens(int max_tokens) {
+    const int prev = pn::gemv_max_tokens();
+    if (max_tokens >= 0) pn::set_gemv_max_tokens(max_tokens);
+    return prev;
+}
+
 size_t pn_linear_workspace_size(int kind, int64_t M, int64_t N, int64_t K) {
     return pn::linear_workspace_bytes(kind, M, N, K, k_packs(K));
 }
@@ -227,6 +233,10 @@ int linear_bf16_impl(const void* x, int64_t M, int64_t K, const int32_t* packed,
     if (M > 64 && (K % 8 != 0 || !aligned(x, 16))) {
         cudaError_t e = pn::launch_linear_simt_bf16(a, (cudaStream_t)stream);
         return e == cudaSuccess ? ok() : cuda_fail(e, "pn_linear_bf16 (cuda-core)");
+    }
+    if (pn::gemv_takes(a)) {
+        cudaError_t e = pn::launch_gemv(a, (cudaStream_t)stream);
+        return e == cudaSuccess ? ok() : cuda_fail(e, "pn_linear_bf16 (decode GEMV)");
     }
     cudaError_t ce;
     const char* why;

@@ -1165,7 +1165,10 @@ static WsLayout ws_layout(int kind, int64_t M, int64_t N, int64_t K, bool allow_
 }
 size_t linear_workspace_bytes(int kind, int64_t M, int64_t N, int64_t K, int64_t packed_ld) {
     if (M <= 0 || N <= 0) return 0;
-    return ws_layout(kind, M, N, K, true, packed_ld % 4 != 0).total;
+    const size_t tc = ws_layout(kind, M, N, K, true, packed_ld % 4 != 0).total;
+    // bf16 decode batches may run on the CUDA-core GEMV instead (pn_gemv.cu)
+    const size_t gv = kind == PN_BF16 ? gemv_workspace_bytes(M, N, (K + kPerWord - 1) / kPerWord) : 0;
+    return tc > gv ? tc : gv;
 }
 size_t linear_workspace_min_bytes(int kind, int64_t M, int64_t N, int64_t K, int64_t packed_ld) {
     if (M <= 0 || N <= 0) return 0;

@@ -61,4 +61,15 @@ cudaError_t launch_linear_simt_bf16(const LinearArgs& a, cudaStream_t s);
 
 int device_sm_count();
 
+// CUDA-core decode GEMV (pn_gemv.cu) for bf16 products of at most
+// gemv_max_tokens() tokens (settable up to kGemvMaxTokens) whose packed rows
+// sit at a 16-byte pitch; its workspace is gemv_workspace_bytes(M, N, KP).
+constexpr int kGemvMaxTokens = 8;
+constexpr int kGemvMaxTokensDefault = 0;
+int gemv_max_tokens();
+void set_gemv_max_tokens(int m);
+size_t gemv_workspace_bytes(int64_t M, int64_t N, int64_t KP);
+bool gemv_takes(const LinearArgs& a);
+cudaError_t launch_gemv(const LinearArgs& a, cudaStream_t s);
+
 }  // namespace pn

@@ -10,6 +10,7 @@
 #include "pn_norm.cu"
 #include "pn_dqmm.cu"
 #include "pn_simt.cu"
+#include "pn_gemv.cu"
 #include "pn_capi.cu"
 #include "pn_static_ws.cu"
 #include "pn_peer.cu"

@@ -30,7 +30,7 @@ EXPORTS = (
     "pn_linear_bf16_nows", "pn_linear_bf16_epi", "pn_act_i8_pitch", "pn_quant_act_i8", "pn_linear_i8",
     "pn_linear_i8_ld", "pn_linear_i8_epi", "pn_layer_norm",
     "pn_ipc_handle", "pn_ipc_open", "pn_ipc_close",
-    "pn_linear_bf16_peers", "pn_peer_barrier", "pn_peer_barrier_wait",
+    "pn_linear_bf16_peers", "pn_peer_barrier", "pn_peer_barrier_wait", "pn_set_gemv_max_tokens",
 )
 
 _lib = None
@@ -85,6 +85,7 @@ def load() -> ctypes.CDLL:
         "pn_linear_bf16_peers": (I, [P, I64, I64, P, I64, I64, F, P, ctypes.POINTER(P), I, I64, I64, I, P, SZ, P]),
         "pn_peer_barrier": (I, [ctypes.POINTER(P), I, I, P, P]),
         "pn_peer_barrier_wait": (I, [ctypes.POINTER(P), I, I, P, I64, P]),
+        "pn_set_gemv_max_tokens": (I, [I]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -10,6 +10,7 @@ of tests/refmodel.weights, and stores, in eval mode on the CPU:
   * the same under bf16 autocast (the reference's inference precision; CPU
     autocast here), which sets the scale of bf16 rounding noise;
   * the loss of the targets path (logits at every position) in fp32;
+  * the gamma (fp32 mean |W|) the reference computed for each QuantLinear;
   * the logits of tests/refmodel.PentaGPT's fp32 forward, as a check that
     the restatement matches (it is asserted here too).
 """
@@ -61,6 +62,9 @@ def main() -> None:
         out[f"{name}.logits_f32"] = l32[:, 0].numpy().astype(np.float32)
         out[f"{name}.logits_bf16_autocast"] = lbf[:, 0].float().numpy().astype(np.float32)
         out[f"{name}.loss_f32"] = np.array([loss.item()], dtype=np.float64)
+        # the gamma the reference computed for each QuantLinear (named_modules order)
+        out[f"{name}.gammas"] = np.array([float(m.weight.abs().mean().clamp(min=1e-8))
+                                          for m in rm.quant_layers(ref)], dtype=np.float32)
         print(f"{name}: |restated - ref| {d:.2e}, |bf16 autocast - f32| {(lbf.float() - l32).abs().max():.3f}, "
               f"loss {loss.item():.4f}")
     np.savez_compressed(os.path.join(HERE, "pentagpt_ref.npz"), **out)

@@ -44,9 +44,14 @@ class QuantLinear(nn.Module):
         self.in_features, self.out_features, self.mode = fan_in, fan_out, mode
         self.weight = nn.Parameter(torch.empty(fan_out, fan_in))
         self.register_parameter("bias", None)
+        # The reference's gamma is torch's fp32 CPU mean, whose last bit depends
+        # on the machine's summation order; the fixtures record the values the
+        # reference computed, and a test may pin them here.
+        self.fixed_gamma = None
 
     def forward(self, x):
-        gamma = self.weight.abs().mean().clamp(min=1e-8)
+        gamma = (self.weight.abs().mean().clamp(min=1e-8) if self.fixed_gamma is None
+                 else torch.tensor(self.fixed_gamma, dtype=self.weight.dtype, device=self.weight.device))
         lim = 2 if self.mode == "pentanet" else 1
         q = torch.clamp(torch.round(self.weight / gamma), -lim, lim)
         return F.linear(x, (q * gamma - self.weight).detach() + self.weight, self.bias)
@@ -140,6 +145,11 @@ def weights(model: nn.Module, seed: int) -> dict:
     # tied: the token table is the lm_head weight (train_pentagpt.py:116)
     out["transformer.wte.weight"] = out["lm_head.weight"]
     return out
+
+
+def quant_layers(model: nn.Module) -> list:
+    """The QuantLinear modules in named_modules() order (tied ones once)."""
+    return [m for _, m in model.named_modules() if type(m).__name__ == "QuantLinear"]
 
 
 def tokens(cfg: Cfg, batch: int, seq: int, seed: int):
