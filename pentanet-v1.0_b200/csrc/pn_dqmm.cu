@@ -81,6 +81,13 @@ struct Cfg {
     // pre-arranged (permute_x_kernel) and are staged with one bulk copy per k-block.
     static constexpr bool kPerm = KIND == Kind::F16 && BT <= 64;
     static constexpr int kIssuers = BT <= 32 ? 4 : (BT <= 64 ? 2 : 1);
+    // MMA N.  The 8-token decode tile (bf16, up to 8 tokens) runs N = 16 MMAs
+    // over a compact activation image: each slab holds only 8 rows (256 bytes,
+    // one 8-row core-matrix group), so the MMA's second group (rows 8-15, one
+    // stride offset = 256 bytes further) reads the next slab; it feeds
+    // accumulator columns 8-15, which are never read.  Half the bytes per
+    // k-block of the 16-token image, and twice the ring depth.
+    static constexpr int kMmaN = BT < 16 ? 16 : BT;
     static constexpr int kSlabBytes = BT * 32;
     // Activation stage: the k-block's BT rows x kRowBytes.  Staged by TMA as
     // kWide boxes of 128-byte rows (128-byte swizzle) and one box of the
@@ -94,9 +101,10 @@ struct Cfg {
     // permute_x_kernel), multiplied by constant A columns in one extra MMA.
     static constexpr int kXSlabs = kPerm ? T::kSteps + 1 : T::kSteps;
     static constexpr int kXDataBytes = kSlabBytes * kXSlabs;
-    static constexpr int kXStageBytes = (kXDataBytes + 1023) / 1024 * 1024;
+    // (+ the 256 bytes the last slab's second row group reads in a compact image)
+    static constexpr int kXStageBytes = (kXDataBytes + (BT < 16 ? 256 : 0) + 1023) / 1024 * 1024;
     static constexpr int kChunksPerRow = kKB * T::kXElem / 16;      // 16-byte pieces of one row per k-block
-    static constexpr int kDCols = kIssuers * BT;                  // accumulators D_0..D_{kIssuers-1}
+    static constexpr int kDCols = kIssuers * kMmaN;               // accumulators D_0..D_{kIssuers-1}
     static constexpr int kA0 = kDCols < 32 ? 32 : kDCols;         // first A column
     // Ring depths.  Waiters that take turns on k-blocks (unpack groups on the
     // TMEM operand ring and the weight ring, MMA issuers on the operand and
@@ -116,7 +124,8 @@ struct Cfg {
     static constexpr int kSXfit = (kBudget - kSW * kWStageBytes) / kXStageBytes;
     // Up to three activation stages per issuer: a copy is issued when the
     // stage's use kSX k-blocks earlier is done, so deeper rings hide its latency.
-    static constexpr int kSX = (kSXfit > 3 * kIssuers ? 3 * kIssuers : (kSXfit > 8 ? 8 : kSXfit)) / kIssuers * kIssuers;
+    static constexpr int kSXcap = (BT < 16 ? 6 : 3) * kIssuers;
+    static constexpr int kSX = (kSXfit > kSXcap ? kSXcap : (kSXfit > 8 ? 8 : kSXfit)) / kIssuers * kIssuers;
     static constexpr int kBarOff = kSX * kXStageBytes + kSW * kWStageBytes;
     // TMEM columns holding the constant A operand of the correction MMA (decode)
     static constexpr int kConstCol = kA0 + kSA * kAStageCols;
@@ -127,7 +136,7 @@ struct Cfg {
     static_assert(kSW % 2 == 0, "weight ring: two producers, two k-blocks per stage");
     static_assert((kSX * kXStageBytes) % 1024 == 0, "weight stages must stay 1024-byte aligned (128B swizzle)");
     static_assert(kA0 + kSA * kAStageCols + (kPerm ? 8 : 0) <= kTmemCols, "TMEM over-subscribed");
-    static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "token tile");
+    static_assert((BT % 16 == 0 && BT >= 16 && BT <= 256) || (BT == 8 && kPerm), "token tile");
     static_assert(kSmem <= 227 * 1024, "shared memory per block");
     static_assert(kTail == 32 || kTail == 64, "activation tail box");
 };
@@ -495,10 +504,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (issuer < C::kIssuers) {
             uint32_t idesc;
             if constexpr (KIND == Kind::F16)
-                idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BT >> 3) << 17) | ((128u >> 4) << 24);
+                idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(C::kMmaN >> 3) << 17) | ((128u >> 4) << 24);
             else  // A = unsigned 8-bit codes, B = signed int8, D = s32
-                idesc = (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(BT >> 3) << 17) | ((128u >> 4) << 24);
-            const uint32_t d_tmem = tmem_base + issuer * BT;
+                idesc = (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(C::kMmaN >> 3) << 17) | ((128u >> 4) << 24);
+            const uint32_t d_tmem = tmem_base + issuer * C::kMmaN;
             uint32_t it = 0, n_local = 0;
             bool ok = true;
             if constexpr (C::kPerm) {
@@ -877,10 +886,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c0 = 16 * half; c0 < BT; c0 += 16 * kUnpackGroups) {
                 if (m0 + c0 >= p.M) break;  // warp-uniform
                 uint32_t acc[16], v[16];
-                tmem_ld16(tmem_base + lane_base + (it_item % C::kIssuers) * BT + c0, acc);
+                tmem_ld16(tmem_base + lane_base + (it_item % C::kIssuers) * C::kMmaN + c0, acc);
                 tmem_wait_ld();
                 for (int a = 1; a < C::kIssuers && a < g.kb1 - g.kb0; ++a) {
-                    tmem_ld16(tmem_base + lane_base + ((it_item + a) % C::kIssuers) * BT + c0, v);
+                    tmem_ld16(tmem_base + lane_base + ((it_item + a) % C::kIssuers) * C::kMmaN + c0, v);
                     tmem_wait_ld();
 #pragma unroll
                     for (int j = 0; j < 16; ++j) add_into(acc[j], v[j]);
@@ -1104,6 +1113,7 @@ static int64_t w_pitch(int64_t KP) { return (KP + 3) & ~int64_t(3); }
 
 // Token tile for a call: the kernel instantiation launch_kind picks.
 static int token_tile(int kind, int64_t M) {
+    if (kind == PN_BF16 && M <= 8) return 8;
     if (M <= 16) return 16;
     if (M <= 32) return 32;
     if (M <= 64) return 64;
@@ -1383,6 +1393,9 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
 
 template <Kind KIND, bool EPI>
 static int launch_kind(const LinearArgs& a, cudaStream_t s, cudaError_t* err, const char** why) {
+    if constexpr (KIND == Kind::F16) {
+        if (a.M <= 8) return launch_bt<KIND, 8, EPI>(a, s, err, why);
+    }
     if (a.M <= 16) return launch_bt<KIND, 16, EPI>(a, s, err, why);
     if (a.M <= 32) return launch_bt<KIND, 32, EPI>(a, s, err, why);
     if (a.M <= 64) return launch_bt<KIND, 64, EPI>(a, s, err, why);
