@@ -126,12 +126,27 @@ struct Cfg {
     // stage's use kSX k-blocks earlier is done, so deeper rings hide its latency.
     static constexpr int kSXcap = (BT < 16 ? 6 : 3) * kIssuers;
     static constexpr int kSX = (kSXfit > kSXcap ? kSXcap : (kSXfit > 8 ? 8 : kSXfit)) / kIssuers * kIssuers;
+    // 8-token decode tiles: the activation loader copies the activations of
+    // the CTA's first kSX k-blocks (use 0 of every activation stage, as soon
+    // as the pre-pass is done); every later use is copied by the weight
+    // loaders, each weight stage's two k-blocks just before its weight box in
+    // the same TMA queue, so they land ahead of the weights they meet (a
+    // separate loader, queued behind the 16 KB weight boxes, issued one copy
+    // per weight box and fell behind the MMAs).  This needs an activation
+    // ring that outlasts the weight ring's lead (kSX >= 2 kSW + 4: the stage a
+    // weight loader refills was released long before), and a stage's later
+    // uses all fall to one weight-loader warp (kSX / 2 even), which then waits
+    // for every release of that stage in order.  Larger tiles keep the
+    // activation loader for all k-blocks.
+    static constexpr bool kXByWLoader = kPerm && kSX >= 2 * kSW + 4 && (kSX / 2) % 2 == 0;
+    static constexpr int kActEarly = kXByWLoader ? kSX : 0;
     static constexpr int kBarOff = kSX * kXStageBytes + kSW * kWStageBytes;
     // TMEM columns holding the constant A operand of the correction MMA (decode)
     static constexpr int kConstCol = kA0 + kSA * kAStageCols;
     static constexpr int kNumBars = 2 * kSW + 2 * kSX + 2 * kSA + 4 + kIssuers;
     static constexpr int kSmem = kBarOff + kNumBars * 8 + 16 + 1024;  // + tmem slot, abort and last-arriver flags + align slack
     static_assert(kSX >= 2 && kSX % kIssuers == 0, "activation ring");
+    static_assert(!kXByWLoader || kActEarly % 2 == 0, "activation copies by whole weight stages");
     static_assert(kSA >= kAParties && kSA % kAParties == 0 && kSA % (kIssuers * T::kAPerKB) == 0, "TMEM operand ring");
     static_assert(kSW % 2 == 0, "weight ring: two producers, two k-blocks per stage");
     static_assert((kSX * kXStageBytes) % 1024 == 0, "weight stages must stay 1024-byte aligned (128B swizzle)");
@@ -392,7 +407,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // loader warps take alternate stages.
         const int producer = warp - kLoadWarp;
         uint32_t st = 0;  // global stage counter
-        bool ok = true;
+        uint32_t x_first = 0, x_end = 0;  // activation copies this warp issued: CTA k-blocks [x_first, x_end)
+        bool ok = true, x_waited = false;
         const int64_t u_end = range_begin(p, blockIdx.x + 1);
         for (int64_t u = range_begin(p, blockIdx.x); u < u_end && ok;) {
             const Seg g = segment_at(p, u, u_end);
@@ -401,6 +417,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int ws = g.kb0 / 2; ws < g.kb1 / 2; ++ws, ++st) {
                 if ((int)(st & 1) != producer) continue;
                 const int sw = st % C::kSW;
+                if constexpr (C::kXByWLoader) {
+                    if (2 * st >= (uint32_t)C::kActEarly) {
+                        // the two k-blocks' activations (the pre-pass's output)
+                        if (!x_waited) {
+                            asm volatile("griddepcontrol.wait;" ::: "memory");
+                            x_waited = true;
+                            x_first = 2 * st;
+                        }
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const uint32_t c = 2 * st + h;
+                            const int sx = c % C::kSX;
+                            if (!warp_wait(&empty_x[sx], ((c / C::kSX) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                            if (lane == 0) {
+                                mbar_arrive_expect_tx(&full_x[sx], C::kXDataBytes);
+                                bulk_load(smem_x + sx * C::kXStageBytes, p.xperm + (size_t)(2 * ws + h) * C::kXDataBytes,
+                                          C::kXDataBytes, &full_x[sx]);
+                            }
+                            x_end = c + 1;
+                        }
+                        if (!ok) break;
+                    }
+                }
                 if (!warp_wait(&empty_w[sw], ((st / C::kSW) & 1) ^ 1, abort_flag)) { ok = false; break; }
                 if (lane == 0) {
                     mbar_arrive_expect_tx(&full_w[sw], kWStageBytes);
@@ -413,6 +452,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Let every issued copy land before the CTA can exit.
             for (uint32_t j = (st > (uint32_t)C::kSW ? st - C::kSW : 0u); j < st; ++j)
                 if ((int)(j & 1) == producer) mbar_wait_drain(&full_w[j % C::kSW], (j / C::kSW) & 1);
+            // this warp's activation copies: its stages' k-blocks among the last kSX
+            for (uint32_t c = (x_end > (uint32_t)C::kSX && x_end - C::kSX > x_first) ? x_end - C::kSX : x_first;
+                 c < x_end; ++c)
+                if ((int)((c >> 1) & 1) == producer) mbar_wait_drain(&full_x[c % C::kSX], (c / C::kSX) & 1);
         }
     } else if (warp == kXLoadWarp) {
         // -------------------------------------------- activation loader ----
@@ -425,7 +468,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             // (decode tiles read the pre-pass's output: wait for that grid)
             if (C::kPerm) asm volatile("griddepcontrol.wait;" ::: "memory");
             const int64_t u_begin = range_begin(p, blockIdx.x);
-            const uint32_t total = (uint32_t)(2 * (range_begin(p, blockIdx.x + 1) - u_begin));
+            uint32_t total = (uint32_t)(2 * (range_begin(p, blockIdx.x + 1) - u_begin));
+            if (C::kXByWLoader && total > (uint32_t)C::kActEarly) total = C::kActEarly;  // the rest: weight loaders
             const uint32_t P = (uint32_t)(p.n_kb / 2);
             uint32_t cur[C::kIssuers];  // next k-block of each issuer
 #pragma unroll
