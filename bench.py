@@ -653,6 +653,26 @@ def run_profile_epilogue(args):
     print(json.dumps({"profile": "c_fc plain / fused gelu", "M": M, "N": N, "K": K}))
 
 
+def run_profile_gemv(args):
+    """Small case for ncu: the CUDA-core decode GEMV (opt-in path) on the
+    8192->28672 layer at M = 1, three warm-up launches and one measured."""
+    import torch
+    import penta_kernel as pk
+    import penta_native as nat
+    nat.load().pn_set_gemv_max_tokens(8)
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(1)
+    K, N = 8192, 28672
+    w = torch.randn(N, K, device=dev, generator=gen) * 0.02
+    packed, _, s = pk.quantize_and_pack(w)
+    del w
+    x = torch.randn(1, K, device=dev, generator=gen).to(torch.bfloat16)
+    for _ in range(4):
+        pk.penta_linear(x, packed, s, K)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": "CUDA-core GEMV 8192->28672, M=1", "warmup_launches": 3, "launches": 1}))
+
+
 def run_profile_prefill(args):
     """Small case for ncu: the int8 prefill GEMM at M = 4096, K = N = 4096,
     three warm-up launches and one measured launch (activations quantised
@@ -1034,6 +1054,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the int8 prefill secondary measurement")
     ap.add_argument("--profile", action="store_true", help="small fixed case for ncu captures")
     ap.add_argument("--profile-prefill", action="store_true", help="int8 prefill case for ncu captures")
+    ap.add_argument("--profile-gemv", action="store_true", help="CUDA-core decode GEMV case for ncu captures")
     ap.add_argument("--profile-gpt", action="store_true", help="PentaGPT-124M forward for ncu launch lists")
     ap.add_argument("--profile-epilogue", action="store_true", help="plain vs fused-GELU product for ncu")
     args = ap.parse_args()
@@ -1047,6 +1068,9 @@ def main():
         return
     if args.profile_prefill:
         run_profile_prefill(args)
+        return
+    if args.profile_gemv:
+        run_profile_gemv(args)
         return
     if args.profile:
         run_profile_case(args)

@@ -15,9 +15,9 @@
 //
 // Limits and sharing:
 //   * the least scratch a call runs with must be <= kStaticScratchBytes
-//     (4 MiB).  That is the decode activation slab for M <= 64
-//     (ceil(ceil(K/10)/16) rounded up to even x tile x 320 bytes, tile = 16,
-//     32 or 64 tokens: 3.7 MB at K = 28672 and 64 tokens), plus
+//     (4 MiB).  That is the decode activation image for M <= 64
+//     (ceil(ceil(K/10)/16) rounded up to even x tile x 352 bytes, tile = 8,
+//     16, 32 or 64 tokens: 4.06 MB at K = 28672 and 64 tokens), plus
 //     N * round4(K_packs) * 4 bytes when the rows are not 16 bytes apart
 //     (packed_ld % 4 != 0) -- far more than 4 MiB for most layers, so callers
 //     store their weights at the pn_packed_ld(K_packs) stride.  Larger
