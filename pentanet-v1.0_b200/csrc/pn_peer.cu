@@ -37,6 +37,11 @@ __global__ void __launch_bounds__(32) peer_barrier_kernel(PeerFlags f, int world
     // during the exchange: it waits for this grid's completion before it
     // touches memory, and the GEMM after it starts streaming weights.
     asm volatile("griddepcontrol.launch_dependents;");
+    // This kernel is itself a programmatic dependent of the GEMM before it
+    // (so that the chain GEMM -> barrier -> next pre-pass -> next GEMM can
+    // overlap the next GEMM's prologue with this one's tail): nothing is
+    // posted before that grid has completed and its stores are visible.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int lane = threadIdx.x;
     int g = 0;
     if (lane == 0) {
@@ -137,8 +142,16 @@ extern "C" int pn_peer_barrier_wait(int* const* flags, int world, int rank, int*
         f.flags[r] = flags[r];
     }
     if (int st = check_device()) return st;
-    pn::peer_barrier_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(f, world, rank, gen, limit);
-    cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, pn::peer_barrier_kernel, f, world, rank, gen, limit);
     return e == cudaSuccess ? ok() : cuda_fail(e, "pn_peer_barrier");
 }
 
