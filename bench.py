@@ -354,6 +354,16 @@ def run_reference(args):
 
 # ------------------------------------------------------------ our arm -----
 
+def decode_kernel_label() -> str:
+    """Which dqmm instantiations run the decode products (limb path up to the
+    library's current limit, kind::f16 above it)."""
+    import penta_native as nat
+    lim = nat.load().pn_set_limb_max_tokens(-1)
+    parts = [f"pn::dqmm_kernel<L8, 4M columns> + limb_x_kernel for M <= {lim}"] if lim > 0 else []
+    parts.append("pn::dqmm_kernel<F16, BT> + permute_x_kernel" + (f" for M > {lim}" if lim > 0 else ""))
+    return "; ".join(parts)
+
+
 def run_profile_case(args):
     """Small case for ncu --set full: both 70B-class layers (94 MB packed each,
     one copy), one launch each at M = 1, 8, 64, after three warm-up launches."""
@@ -980,7 +990,7 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
                          "traffic_source": traffic_src,
-                         "peak_source": peaks["source"], "kernel": "pn::dqmm_kernel<F16, BT>",
+                         "peak_source": peaks["source"], "kernel": decode_kernel_label(),
                          "per_launch": per},
             "e2e": {"value": round(e2e_val, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps, "eager_value": round(e2e_eager, 1),

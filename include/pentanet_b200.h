@@ -104,6 +104,18 @@ int pn_unpack(const int32_t *packed, int64_t N, int64_t K_packs, int64_t K_orig,
  * counterpart in the reference. */
 int pn_set_gemv_max_tokens(int max_tokens);
 
+/* bf16 products of at most this many tokens (0..16; default 2) with
+ * K <= 65536 run on the limb decode kernel: each token's activations become
+ * 32-bit fixed-point integers (x within 2^-25 max|x| of itself, exact for
+ * every element within a factor 2^17 of the row's largest), split into four
+ * int8 limbs, and the packed codes meet them in kind::i8 MMAs whose int32
+ * sums combine exactly; one fp32 rounding at the end.  Larger batches use the kind::f16 kernel
+ * (bf16 products accumulated in fp32).  A token holding an inf or NaN gives
+ * NaN outputs on the limb path.  Sets the limit when max_tokens >= 0 and
+ * returns the previous one.  Process-wide.  No counterpart in the
+ * reference. */
+int pn_set_limb_max_tokens(int max_tokens);
+
 /* Recommended workspace bytes for pn_linear_bf16 / pn_linear_i8 at this shape
  * (0 allowed when the result is 0).  kind: PN_BF16 or PN_I8.  With this much
  * the kernel may split one output tile's K range over several SMs when there

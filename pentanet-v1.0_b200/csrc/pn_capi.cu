@@ -170,6 +170,12 @@ int pn_set_gemv_max_tokens(int max_tokens) {
     return prev;
 }
 
+int pn_set_limb_max_tokens(int max_tokens) {
+    const int prev = pn::l8_max_tokens();
+    if (max_tokens >= 0) pn::set_l8_max_tokens(max_tokens);
+    return prev;
+}
+
 size_t pn_linear_workspace_size(int kind, int64_t M, int64_t N, int64_t K) {
     return pn::linear_workspace_bytes(kind, M, N, K, k_packs(K));
 }

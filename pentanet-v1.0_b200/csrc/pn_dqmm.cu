@@ -47,7 +47,11 @@ constexpr int kMaxIssuers = 4;
 constexpr int kThreads = 32 * (kUnpackWarps + 3 + kMaxIssuers);
 constexpr int kTmemCols = 512;
 
-enum class Kind { F16, I8 };
+// F16: bf16 activations, kind::f16 MMAs.  I8: int8 activations (per-token
+// absmax quantised), kind::i8.  L8: bf16 activations of a decode batch (at
+// most 16 tokens) as four int8 limbs of a per-token 32-bit fixed-point
+// integer, kind::i8 (see limb_x_kernel).
+enum class Kind { F16, I8, L8 };
 
 template <Kind KIND>
 struct KindT;
@@ -67,6 +71,32 @@ struct KindT<Kind::I8> {
     static constexpr int kACols = 40;      // 4 codes per column
     static constexpr int kAPerKB = 1;
 };
+template <>
+struct KindT<Kind::L8> : KindT<Kind::I8> {};
+
+// Limb decode (Kind::L8): a token occupies four accumulator columns (its
+// four limbs), so a 16-column epilogue chunk holds 4 tokens.
+constexpr int kL8Cols = 4;
+constexpr int kL8MaxTokens = 16;
+// Default limit of pn_set_limb_max_tokens: the limb path is faster than the
+// kind::f16 decode kernel on the compact 8-column tile (1-2 tokens: 30.0 vs
+// 33.8 us per 94 MB product on B200) and slower on the wider tiles.
+constexpr int kL8DefaultTokens = 2;
+constexpr int kL8MaxK = 65536;  // keeps every limb accumulator inside int32 (|A| <= 224, |limb| <= 128)
+constexpr int kL8NonFinite = -0x7fffffff - 1;  // lx_shift of a token holding an inf or NaN
+
+// v * 2^e for e in [-252, 254], as at most two products by normal powers of
+// two (exact unless the result is subnormal).
+__device__ __forceinline__ float scale_pow2(float v, int e) {
+    if (e < -126) {
+        v = __fmul_rn(v, 0x1p-126f);
+        e += 126;
+    } else if (e > 127) {
+        v = __fmul_rn(v, 0x1p127f);
+        e -= 127;
+    }
+    return __fmul_rn(v, __int_as_float((127 + e) << 23));
+}
 
 template <Kind KIND, int BT>
 struct Cfg {
@@ -78,8 +108,16 @@ struct Cfg {
     // cycles, so two issuers keep the tensor pipe busy; large tiles use one.
     static constexpr bool kXTma = BT >= 128;
     // bf16 decode tiles use the permuted unpack; their activations come
-    // pre-arranged (permute_x_kernel) and are staged with one bulk copy per k-block.
-    static constexpr bool kPerm = KIND == Kind::F16 && BT <= 64;
+    // pre-arranged (permute_x_kernel / limb_x_kernel) and are staged with one
+    // bulk copy per k-block.
+    static constexpr bool kL8 = KIND == Kind::L8;
+    static constexpr bool kPerm = (KIND == Kind::F16 && BT <= 64) || kL8;
+    // kind::f16 decode tiles add the code offset through one extra MMA per
+    // k-block (constant A columns x a correction slab); limb tiles subtract it
+    // in the epilogue.
+    static constexpr bool kCorr = KIND == Kind::F16 && kPerm;
+    // accumulator columns per token: BT counts columns, BT / kCPT tokens
+    static constexpr int kCPT = kL8 ? kL8Cols : 1;
     static constexpr int kIssuers = BT <= 32 ? 4 : (BT <= 64 ? 2 : 1);
     // MMA N.  The 8-token decode tile (bf16, up to 8 tokens) runs N = 16 MMAs
     // over a compact activation image: each slab holds only 8 rows (256 bytes,
@@ -99,7 +137,7 @@ struct Cfg {
     static constexpr int kTail = kRowBytes % 128;
     // Decode stages carry one more slab: the k-block's offset correction (see
     // permute_x_kernel), multiplied by constant A columns in one extra MMA.
-    static constexpr int kXSlabs = kPerm ? T::kSteps + 1 : T::kSteps;
+    static constexpr int kXSlabs = kCorr ? T::kSteps + 1 : T::kSteps;
     static constexpr int kXDataBytes = kSlabBytes * kXSlabs;
     // (+ the 256 bytes the last slab's second row group reads in a compact image)
     static constexpr int kXStageBytes = (kXDataBytes + (BT < 16 ? 256 : 0) + 1023) / 1024 * 1024;
@@ -150,8 +188,9 @@ struct Cfg {
     static_assert(kSA >= kAParties && kSA % kAParties == 0 && kSA % (kIssuers * T::kAPerKB) == 0, "TMEM operand ring");
     static_assert(kSW % 2 == 0, "weight ring: two producers, two k-blocks per stage");
     static_assert((kSX * kXStageBytes) % 1024 == 0, "weight stages must stay 1024-byte aligned (128B swizzle)");
-    static_assert(kA0 + kSA * kAStageCols + (kPerm ? 8 : 0) <= kTmemCols, "TMEM over-subscribed");
+    static_assert(kA0 + kSA * kAStageCols + (kCorr ? 8 : 0) <= kTmemCols, "TMEM over-subscribed");
     static_assert((BT % 16 == 0 && BT >= 16 && BT <= 256) || (BT == 8 && kPerm), "token tile");
+    static_assert(!kL8 || BT <= 64, "limb tiles: at most 16 tokens");
     static_assert(kSmem <= 227 * 1024, "shared memory per block");
     static_assert(kTail == 32 || kTail == 64, "activation tail box");
 };
@@ -185,6 +224,12 @@ struct DqmmParams {
     int32_t* acc_out;
     const float* s_x;
     const int32_t* rowsum;
+    // limb decode (Kind::L8), written by limb_x_kernel: per token its
+    // fixed-point exponent S (kL8NonFinite when a value is inf or NaN) and
+    // the partial sums of its offset correction, lx_chunks per token
+    const int* lx_shift;
+    const long long* lx_corr;
+    int lx_chunks;
 };
 
 // (a & M) | C as one LOP3.  Written out because the compiler otherwise emits
@@ -249,6 +294,37 @@ __device__ __forceinline__ void unpack_word_bf16_perm(uint32_t p, uint32_t* r) {
     r[2] = r2 & 0x00380070u;  // code 2 at bit 4, code 7 at bit 19
     r[3] = r8 & 0x0007000Eu;  // code 3 at bit 1, code 8 at bit 16
     r[4] = r8 & 0x00380070u;  // code 4 at bit 4, code 9 at bit 19
+}
+
+// Limb decode (Kind::L8): unsigned 8-bit A operands of two packed words (20
+// weights) in five registers, one mask per four codes.  Each byte holds one
+// code c in place, shifted left by t = (its bit offset in the word) minus
+// (the byte's offset), so the byte's value is c * 2^t (t <= 5: at most 224
+// for a 3-bit field).  Register 0 (word p): codes 0, 3, 6, 8 with t = 0, 1,
+// 2, 0; register 1: codes 1, 4, 7, 9 with t = 3, 4, 5, 3; registers 2-3 the
+// same for word q; register 4: codes 2 and 5 of p, then of q, t = 0, 1, 0, 1.
+// MMA position r (0..19) of the pair therefore multiplies the weight at k
+// offset l8_src(r) (0-9 in p, 10-19 in q) by 2^l8_shift(r); limb_x_kernel
+// scales that activation by 2^-l8_shift(r) to match.
+__host__ __device__ constexpr int l8_src(int r) {
+    // {0,3,6,8, 1,4,7,9, 10,13,16,18, 11,14,17,19, 2,5,12,15}
+    return r < 16 ? (r & 8 ? 10 : 0) + ((r & 4) ? (int)((0x9741u >> (4 * (r & 3))) & 0xF)
+                                               : (int)((0x8630u >> (4 * (r & 3))) & 0xF))
+                  : (int)((0xFC52u >> (4 * (r - 16))) & 0xF);
+}
+__host__ __device__ constexpr int l8_shift(int r) {
+    // {0,1,2,0, 3,4,5,3, 0,1,2,0, 3,4,5,3, 0,1,0,1}
+    return r < 16 ? ((r & 4) ? (int)((0x3543u >> (4 * (r & 3))) & 0xF) : (int)((0x0210u >> (4 * (r & 3))) & 0xF))
+                  : (r & 1);
+}
+__device__ __forceinline__ void unpack_pair_l8(uint32_t p, uint32_t q, uint32_t* r) {
+    r[0] = p & 0x071C0E07u;
+    r[1] = p & 0x38E07038u;
+    r[2] = q & 0x071C0E07u;
+    r[3] = q & 0x38E07038u;
+    // (p >> 6): code 2 -> bits 0-2, code 5 -> bits 9-11; (q << 10): code 2 ->
+    // bits 16-18, code 5 -> bits 25-27; the left shift as a multiply (FMA pipe)
+    r[4] = and_or_r<0x00000E07u>(p >> 6, (q * 1024u) & 0x0E070000u);
 }
 
 // Unsigned codes of two packed words (20 weights) as five int8x4 registers in
@@ -366,24 +442,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     // prologue and weight streaming on the SMs this grid frees.
     asm volatile("griddepcontrol.launch_dependents;");
 
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < C::kSW; ++s) {
+    // Barrier setup spread over warp 0's lanes (one thread initialising the
+    // ~90 barriers serially took ~2000 cycles before the first weight load).
+    if (warp == 0) {
+        for (int s = lane; s < C::kSW; s += 32) {
             mbar_init(&full_w[s], 1);
             mbar_init(&empty_w[s], 8);  // 2 k-blocks x 4 lane quarters
         }
-        for (int s = 0; s < C::kSX; ++s) {
+        for (int s = lane; s < C::kSX; s += 32) {
             mbar_init(&full_x[s], 1);
             mbar_init(&empty_x[s], 1);
         }
-        for (int s = 0; s < C::kSA; ++s) {
+        for (int s = lane; s < C::kSA; s += 32) {
             mbar_init(&full_a[s], 4);
             mbar_init(&empty_a[s], 1);
         }
-        mbar_init(acc_full, C::kIssuers);
-        mbar_init(acc_empty, kUnpackWarps);
-        for (int i = 0; i < C::kIssuers; ++i) mbar_init(&drain[i], 1);
-        mbar_init(const_bar, 4);
-        *abort_flag = 0;
+        if (lane < C::kIssuers) mbar_init(&drain[lane], 1);
+        if (lane == 0) {
+            mbar_init(acc_full, C::kIssuers);
+            mbar_init(acc_empty, kUnpackWarps);
+            mbar_init(const_bar, 4);
+            *abort_flag = 0;
+        }
         fence_barrier_init();
     }
     if (warp == kMmaWarp) {
@@ -554,7 +634,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t d_tmem = tmem_base + issuer * C::kMmaN;
             uint32_t it = 0, n_local = 0;
             bool ok = true;
-            if constexpr (C::kPerm) {
+            if constexpr (C::kCorr) {
                 ok = warp_wait(const_bar, 0, abort_flag);
                 tc_fence_after();
             }
@@ -600,12 +680,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 hi[j] = kDescHiSW64;
                             }
                         }
-                        if (C::kPerm && hh == T::kAPerKB - 1) {
+                        if (C::kCorr && hh == T::kAPerKB - 1) {
                             // + the k-block's offset correction: constant A columns x slab kSteps
                             mma5c_ts_warp(d_tmem, a_col, lo, hi, tmem_base + C::kConstCol,
                                           xs_lo + ((T::kSteps * C::kSlabBytes) >> 4), idesc, first ? 0u : 1u);
                         } else {
-                            mma5_ts_warp<KIND == Kind::I8>(d_tmem, a_col, lo, hi, idesc, first ? 0u : 1u);
+                            mma5_ts_warp<KIND != Kind::F16>(d_tmem, a_col, lo, hi, idesc, first ? 0u : 1u);
                         }
                         first = false;
                         // the stage is free for its group once these MMAs are done
@@ -638,7 +718,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int half = warp >> 2;  // warp group within the quarter
         const int row = quarter * 32 + lane;
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-        if constexpr (C::kPerm) {
+        if constexpr (C::kCorr) {
             // Constant A operand of the correction MMA: 1.0 at K positions 0-2
             // of every row (bf16 pairs: column 0 = (1, 1), column 1 = (1, 0)).
             if (half == 0) {
@@ -662,7 +742,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const Seg g = segment_at(p, u, u_end);
             u += (g.kb1 - g.kb0) / 2;
             const int64_t n0 = (int64_t)(g.tile % p.n_row_tiles) * kRows;
-            const int m0 = (g.tile / p.n_row_tiles) * BT;
+            // first token of the tile, and the tile's accumulator columns that
+            // carry tokens (kCPT columns per token)
+            const int m0 = (g.tile / p.n_row_tiles) * (BT / C::kCPT);
+            const int ncol = (p.M - m0) * C::kCPT < BT ? (p.M - m0) * C::kCPT : BT;
             const uint32_t it_item = it;
             // this group's k-blocks of the segment: global index == half (mod 4)
             const int nkb = g.kb1 - g.kb0;
@@ -689,13 +772,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int hh = 0; hh < T::kAPerKB; ++hh) {
                     // Words are read from shared memory only when needed (8 per bf16
                     // half, all 16 for int8), which keeps register pressure down; the
-                    // weight stage is released after the last read.
+                    // weight stage is released right after the last read.
                     uint32_t wa[8], wb[8];
                     if constexpr (KIND == Kind::F16) {
                         load8(hh, wa);
                     } else {
                         load8(0, wa);
                         load8(1, wb);
+                    }
+                    if (hh == T::kAPerKB - 1) {
+                        // The k-block's words are in registers: its half of the
+                        // weight stage is free for the loader now.
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&empty_w[sw]);
                     }
                     const uint32_t ua = ik * T::kAPerKB + hh;  // operand stage use
                     const int sa = ua % C::kSA;
@@ -714,8 +803,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         // 8 word pairs -> 40 columns
 #pragma unroll
                         for (int w = 0; w < 4; ++w) {
-                            unpack_pair_u8(wa[2 * w], wa[2 * w + 1], &cols[5 * w]);
-                            unpack_pair_u8(wb[2 * w], wb[2 * w + 1], &cols[20 + 5 * w]);
+                            if constexpr (C::kL8) {
+                                unpack_pair_l8(wa[2 * w], wa[2 * w + 1], &cols[5 * w]);
+                                unpack_pair_l8(wb[2 * w], wb[2 * w + 1], &cols[20 + 5 * w]);
+                            } else {
+                                unpack_pair_u8(wa[2 * w], wa[2 * w + 1], &cols[5 * w]);
+                                unpack_pair_u8(wb[2 * w], wb[2 * w + 1], &cols[20 + 5 * w]);
+                            }
                         }
                     }
                     // The stage is free once the MMAs of its previous use are done
@@ -738,10 +832,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) {
-                        mbar_arrive(&full_a[sa]);
-                        if (hh == T::kAPerKB - 1) mbar_arrive(&empty_w[sw]);
-                    }
+                    if (lane == 0) mbar_arrive(&full_a[sa]);
                 }
                 if (!ok) break;
             }
@@ -766,7 +857,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 return __fmul_rn(v, p.scale);
             };
             // Fixed-point unit of the split-tile sums (2^-24 of an output unit).
-            constexpr float kFix = C::kPerm ? 0x1p91f : kFixScale;
+            constexpr float kFix = C::kCorr ? 0x1p91f : kFixScale;
             // Final epilogue of 16 accumulator columns starting at c0.
             // MULTI: output-sharded layers store into every GPU's buffer; the
             // common single-output case is compiled separately.
@@ -891,21 +982,66 @@ __global__ void __launch_bounds__(kThreads, 1)
                                    (!EPI || (p.residual == nullptr && p.act == kActNone));
             const bool fast_out = p.n_out == 1 && plain_out;
             const bool epi_out = EPI && p.n_out == 1 && !p.y_f32 && p.acc_out == nullptr && !plain_out;
-            auto finish = [&](int c0, const uint32_t (&acc)[16]) {
-                if constexpr (EPI) {
-                    if (epi_out && m0 + c0 + 16 <= p.M) {
-                        finish_epi(c0, acc);
-                        return;
+            // Limb decode: a chunk holds 4 tokens; token j's limb sums D0..D3
+            // (columns 4j..4j+3) combine exactly as D0 + 2^8 D1 + 2^16 D2 +
+            // 2^24 D3 in 64 bits, minus twice its offset correction; then one
+            // conversion to fp32, the exact power-of-two rescale 2^-S and the
+            // weight scale.
+            auto finish_l8 = [&](int c0, const uint32_t (&acc)[16]) {
+                if (n >= p.N) return;
+#pragma unroll
+                for (int j = 0; j < 16 / kL8Cols; ++j) {
+                    const int m = m0 + c0 / kL8Cols + j;
+                    if (m >= p.M) break;
+                    const int sh = __ldcg(p.lx_shift + m);
+                    float yv;
+                    if (sh == kL8NonFinite) {
+                        yv = __int_as_float(0x7fc00000);
+                    } else {
+                        long long corr = 0;
+                        for (int c = 0; c < p.lx_chunks; ++c) corr += __ldcg(p.lx_corr + (size_t)m * p.lx_chunks + c);
+                        const long long r = (long long)(int)acc[kL8Cols * j] +
+                                            (long long)(int)acc[kL8Cols * j + 1] * 256 +
+                                            (long long)(int)acc[kL8Cols * j + 2] * 65536 +
+                                            (long long)(int)acc[kL8Cols * j + 3] * 16777216 - 2 * corr;
+                        yv = __fmul_rn(scale_pow2(__ll2float_rn(r), -sh), p.scale);
+                    }
+                    if (p.n_out == 0) continue;
+                    const __nv_bfloat16* res = nullptr;
+                    int act = kActNone;
+                    if constexpr (EPI) {
+                        if (p.residual) res = p.residual + (int64_t)m * p.ld_res + n;
+                        act = p.act;
+                    }
+                    const int64_t off = (int64_t)m * p.ld_y + p.y_col0 + n;
+                    if (p.y_f32) {
+                        yv = epilogue_f32(yv, p.bias, bias_f, act, res);
+                        for (int r = 0; r < p.n_out; ++r) static_cast<float*>(p.y_out[r])[off] = yv;
+                    } else {
+                        const __nv_bfloat16 t = epilogue_bf16(yv, p.bias, bias_f, act, res);
+                        for (int r = 0; r < p.n_out; ++r) static_cast<__nv_bfloat16*>(p.y_out[r])[off] = t;
                     }
                 }
-                if (fast_out && m0 + c0 + 16 <= p.M)
-                    finish_fast(c0, acc);
-                else if (p.n_out > 1 && plain_out && m0 + c0 + 16 <= p.M)
-                    finish_fast_multi(c0, acc);
-                else if (p.n_out > 1)
-                    finish_t(std::true_type{}, c0, acc);
-                else
-                    finish_t(std::false_type{}, c0, acc);
+            };
+            auto finish = [&](int c0, const uint32_t (&acc)[16]) {
+                if constexpr (C::kL8) {
+                    finish_l8(c0, acc);
+                } else {
+                    if constexpr (EPI) {
+                        if (epi_out && m0 + c0 + 16 <= p.M) {
+                            finish_epi(c0, acc);
+                            return;
+                        }
+                    }
+                    if (fast_out && m0 + c0 + 16 <= p.M)
+                        finish_fast(c0, acc);
+                    else if (p.n_out > 1 && plain_out && m0 + c0 + 16 <= p.M)
+                        finish_fast_multi(c0, acc);
+                    else if (p.n_out > 1)
+                        finish_t(std::true_type{}, c0, acc);
+                    else
+                        finish_t(std::false_type{}, c0, acc);
+                }
             };
             auto add_into = [&](uint32_t& d, uint32_t v) {
                 if constexpr (KIND == Kind::F16)
@@ -928,7 +1064,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // This thread's accumulator columns: chunks c0 = 16*half + 64*i.
 #pragma unroll 1
             for (int c0 = 16 * half; c0 < BT; c0 += 16 * kUnpackGroups) {
-                if (m0 + c0 >= p.M) break;  // warp-uniform
+                if (c0 >= ncol) break;  // warp-uniform
                 uint32_t acc[16], v[16];
                 tmem_ld16(tmem_base + lane_base + (it_item % C::kIssuers) * C::kMmaN + c0, acc);
                 tmem_wait_ld();
@@ -944,7 +1080,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // (griddepcontrol.wait above: the decode pre-pass zeroed the sums)
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        if (m0 + c0 + j >= p.M) break;
+                        if (c0 + j >= ncol) break;
                         if constexpr (KIND == Kind::F16)
                             red_add(static_cast<long long*>(p.accbuf) + acc_base + (size_t)(c0 + j) * kRows,
                                     __float2ll_rn(__uint_as_float(acc[j]) * kFix));
@@ -982,13 +1118,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __threadfence();
 #pragma unroll 1
                     for (int c0 = 16 * half; c0 < BT; c0 += 16 * kUnpackGroups) {
-                        if (m0 + c0 >= p.M) break;
+                        if (c0 >= ncol) break;
                         uint32_t acc[16];
                         if constexpr (kRedSum) {
 #pragma unroll
                             for (int j = 0; j < 16; ++j) {
                                 acc[j] = 0;
-                                if (m0 + c0 + j < p.M) {
+                                if (c0 + j < ncol) {
                                     if constexpr (KIND == Kind::F16) {
                                         const long long v =
                                             __ldcg(static_cast<const long long*>(p.accbuf) + acc_base + (size_t)(c0 + j) * kRows);
@@ -1116,6 +1252,140 @@ __global__ void __launch_bounds__(kPermThreads) permute_x_kernel(const __nv_bflo
     }
 }
 
+// Limb decode pre-pass: writes a decode batch's bf16 activations as the GEMM
+// kernel's shared-memory image of its int8 B operand.
+//
+// Per token m: E with max|x_m| < 2^E (from the largest bf16 magnitude), the
+// fixed-point exponent S = 30 - E, and for every k the integer
+// X_k = round_half_even(x_k * 2^(S - t_k)), |X_k| <= 2^30, where t_k is the
+// shift its weight carries in the A operand (unpack_pair_l8).  X_k is split
+// into balanced base-256 limbs X = L0 + 2^8 L1 + 2^16 L2 + 2^24 L3, each in
+// [-128, 127], stored in the B rows (accumulator columns) 4m .. 4m+3; the MMAs
+// then sum c_k 2^t_k L_l,k exactly in int32 per limb.  The code offset enters
+// as corr_m = sum_k 2^t_k X_k (exact, int64), from which the epilogue forms
+// sum_k (c_k - 2) 2^t_k X_k = sum_k q_k x~_k 2^S, x~_k being x_k rounded to a
+// multiple of 2^(t_k - S) <= 2^(E - 25): at most 2^-25 max|x_m| away, and
+// exact for every element within a factor 2^17 of the row's largest magnitude.
+//
+// Layout: per k-block 5 slabs (MMA K-steps of 32 k) of BT rows x 32 bytes,
+// 32-byte swizzled; MMA position r of a k-block holds k = 20 (r / 20) +
+// l8_src(r % 20).  Rows of tokens >= M are not written (their accumulator
+// columns are never read back).
+//
+// Grid (chunks + zeroing blocks, M); each chunk block reduces the token's
+// whole row for max|x| (the row is in L2: the redundant reads are cheap at
+// decode sizes), then writes kb_per_chunk k-blocks, one thread per 4 MMA
+// positions, and its partial correction to lx_corr[m][chunk].
+constexpr int kLimbThreads = 256;
+template <int BT>
+__global__ void __launch_bounds__(kLimbThreads) limb_x_kernel(const __nv_bfloat16* __restrict__ x, int M, int K,
+                                                               int n_kb, int kb_per_chunk, int n_chunks,
+                                                               uint8_t* __restrict__ out, int* __restrict__ lx_shift,
+                                                               long long* __restrict__ lx_corr,
+                                                               uint4* __restrict__ zero, int64_t n_zero16) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    // the GEMM's split-tile counters and sums start at zero
+    {
+        const int64_t b = (int64_t)blockIdx.y * gridDim.x + blockIdx.x;
+        const int64_t nthr = (int64_t)gridDim.x * gridDim.y * kLimbThreads;
+        for (int64_t i = b * kLimbThreads + threadIdx.x; i < n_zero16; i += nthr) zero[i] = make_uint4(0, 0, 0, 0);
+    }
+    const int ch = blockIdx.x;
+    if (ch >= n_chunks) return;  // zeroing-only block
+    const int m = blockIdx.y;
+    const __nv_bfloat16* xr = x + (size_t)m * K;
+    const uint16_t* xs = reinterpret_cast<const uint16_t*>(xr);
+
+    // max |x| of the row as bf16 magnitude bits (ordered like the values;
+    // 0x7F80 and above: inf or NaN)
+    uint32_t mx = 0;
+    if ((reinterpret_cast<uintptr_t>(xr) & 15) == 0) {
+        const int nv = K >> 3;
+        const uint4* xv = reinterpret_cast<const uint4*>(xr);
+        for (int i = threadIdx.x; i < nv; i += kLimbThreads) {
+            const uint4 v = __ldg(xv + i);
+            uint32_t t = __vmaxu2(__vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu),
+                                  __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu));
+            t = max(t & 0xFFFFu, t >> 16);
+            mx = max(mx, t);
+        }
+        for (int k = (nv << 3) + threadIdx.x; k < K; k += kLimbThreads) mx = max(mx, (uint32_t)(__ldg(xs + k) & 0x7FFFu));
+    } else {
+        for (int k = threadIdx.x; k < K; k += kLimbThreads) mx = max(mx, (uint32_t)(__ldg(xs + k) & 0x7FFFu));
+    }
+    __shared__ uint32_t red_u[kLimbThreads / 32];
+    __shared__ long long red_ll[kLimbThreads / 32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red_u[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = red_u[0];
+#pragma unroll
+    for (int w = 1; w < kLimbThreads / 32; ++w) mx = max(mx, red_u[w]);
+
+    const bool finite = mx < 0x7F80u;
+    // max|x| < 2^E; E = -126 covers zero and subnormal maxima
+    const int ebits = (int)(mx >> 7);
+    const int E = ebits == 0 ? -126 : ebits - 126;
+    const int S = 30 - E;
+    if (ch == 0 && threadIdx.x == 0) lx_shift[m] = finite ? S : kL8NonFinite;
+
+    constexpr int kSlab = BT * 32;
+    constexpr int kStage = 5 * kSlab;
+    const uint32_t flip = (uint32_t)(m & 1) << 4;  // 32-byte swizzle: rows 4m..4m+3 share (row >> 2) & 1 = m & 1
+    uint8_t* const rows = out + (size_t)m * 4 * 32;
+    long long corr = 0;
+    const int kb0 = ch * kb_per_chunk;
+    const int kb1 = min(n_kb, kb0 + kb_per_chunk);
+    const int nq = (kb1 - kb0) * (kKB / 4);  // 40 quads of MMA positions per k-block
+    for (int qi = threadIdx.x; qi < nq; qi += kLimbThreads) {
+        const int kb = kb0 + qi / (kKB / 4);
+        const int qk = qi - (kb - kb0) * (kKB / 4);  // quad within the k-block
+        uint32_t w0 = 0, w1 = 0, w2 = 0, w3 = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int r = 4 * qk + i;          // MMA position in the k-block
+            const int pr = r / 20, rr = r - 20 * (r / 20);
+            const int t = l8_shift(rr);
+            const int k = kb * kKB + 20 * pr + l8_src(rr);
+            int X = 0;
+            if (finite && k < K) {
+                const float xf = __uint_as_float((uint32_t)__ldg(xs + k) << 16);
+                X = __float2int_rn(scale_pow2(xf, S - t));
+            }
+            corr += (long long)X * (1 << t);
+            const int l0 = (int)(int8_t)X;
+            const int x1 = (X - l0) >> 8;
+            const int l1 = (int)(int8_t)x1;
+            const int x2 = (x1 - l1) >> 8;
+            const int l2 = (int)(int8_t)x2;
+            const int l3 = (x2 - l2) >> 8;
+            w0 |= (uint32_t)(l0 & 0xFF) << (8 * i);
+            w1 |= (uint32_t)(l1 & 0xFF) << (8 * i);
+            w2 |= (uint32_t)(l2 & 0xFF) << (8 * i);
+            w3 |= (uint32_t)(l3 & 0xFF) << (8 * i);
+        }
+        // slab qk / 8, bytes 4 (qk % 8) .. +3 of each limb row
+        const uint32_t b = 4u * (uint32_t)(qk & 7);
+        uint8_t* const dst = rows + (size_t)kb * kStage + (qk >> 3) * kSlab + ((((b >> 4) << 4) ^ flip) | (b & 15));
+        *reinterpret_cast<uint32_t*>(dst) = w0;
+        *reinterpret_cast<uint32_t*>(dst + 32) = w1;
+        *reinterpret_cast<uint32_t*>(dst + 64) = w2;
+        *reinterpret_cast<uint32_t*>(dst + 96) = w3;
+    }
+    // the block's correction partial (integer sums: order-independent)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) corr += __shfl_xor_sync(0xffffffffu, corr, o);
+    if ((threadIdx.x & 31) == 0) red_ll[threadIdx.x >> 5] = corr;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        long long t = 0;
+#pragma unroll
+        for (int w = 0; w < kLimbThreads / 32; ++w) t += red_ll[w];
+        lx_corr[(size_t)m * n_chunks + ch] = t;
+    }
+}
+
 // ------------------------------------------------------------------ host ----
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -1142,7 +1412,18 @@ int device_sm_count() {
     return n;
 }
 
-static int decode_tile(int64_t M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
+// Limb decode (Kind::L8) takes bf16 products of at most g_l8_max_tokens
+// tokens (settable, 0 = off) with K <= kL8MaxK.
+static int g_l8_max_tokens = kL8DefaultTokens;
+int l8_max_tokens() { return g_l8_max_tokens; }
+void set_l8_max_tokens(int m) { g_l8_max_tokens = m < 0 ? 0 : (m > kL8MaxTokens ? kL8MaxTokens : m); }
+static bool l8_shape(int kind, int64_t M, int64_t K) {
+    return kind == PN_BF16 && M >= 1 && M <= kL8MaxTokens && K <= kL8MaxK;
+}
+static bool l8_takes(int kind, int64_t M, int64_t K) { return l8_shape(kind, M, K) && M <= g_l8_max_tokens; }
+// accumulator columns of a limb tile: 4 per token
+static int l8_tile(int64_t M) { return M <= 2 ? 8 : (M <= 4 ? 16 : (M <= 8 ? 32 : 64)); }
+constexpr int kL8KbPerChunk = 16;  // k-blocks per limb_x_kernel block
 
 // k-blocks per item: enough to cover the packed words, rounded up to even so
 // that weight stages (2 k-blocks each) never straddle items.  The padding block
@@ -1175,18 +1456,22 @@ static int token_tile(int kind, int64_t M) {
 // Tiles split across CTAs only while there are few of them per SM; with many
 // tiles whole-tile ranges already balance to within one tile.
 struct WsLayout {
-    size_t xperm, wpitch, counters, accbuf, zero_bytes, total;
+    size_t xperm, wpitch, counters, accbuf, zero_bytes, total, lx_shift, lx_corr;
     int64_t n_items, total_pairs;
-    int grid, bt, n_kb, unit, acc_cols;
+    int grid, bt, n_kb, unit, acc_cols, n_chunks;
 };
 // repitch: the packed rows are not 16 bytes apart (packed_ld % 4 != 0), so a
 // 16-byte-pitch copy of the whole matrix is part of the workspace.
-static WsLayout ws_layout(int kind, int64_t M, int64_t N, int64_t K, bool allow_split, bool repitch) {
+// l8: the limb decode layout (limb image, per-token exponents and correction
+// partials; BT counts accumulator columns, four per token).
+static WsLayout ws_layout_ex(int kind, int64_t M, int64_t N, int64_t K, bool allow_split, bool repitch, bool l8) {
     WsLayout w{};
     const int64_t KP = (K + kPerWord - 1) / kPerWord;
-    w.bt = token_tile(kind, M);
+    w.bt = l8 ? l8_tile(M) : token_tile(kind, M);
+    const int cpt = l8 ? kL8Cols : 1;
     w.n_kb = n_kblocks(KP);
-    w.n_items = ((N + kRows - 1) / kRows) * ((M + w.bt - 1) / w.bt);
+    w.n_chunks = l8 ? (w.n_kb + kL8KbPerChunk - 1) / kL8KbPerChunk : 0;
+    w.n_items = ((N + kRows - 1) / kRows) * ((M * cpt + w.bt - 1) / w.bt);
     w.total_pairs = w.n_items * (w.n_kb / 2);
     int sms = device_sm_count();
     if (sms <= 0) sms = 148;
@@ -1196,10 +1481,18 @@ static WsLayout ws_layout(int kind, int64_t M, int64_t N, int64_t K, bool allow_
     w.grid = (int)(units < sms ? units : sms);
     size_t off = 0;
     w.xperm = off;
-    if (kind == PN_BF16 && M >= 1 && M <= 64) off += round256((size_t)w.n_kb * w.bt * 32 * 11);
+    if (l8) {
+        off += round256((size_t)w.n_kb * w.bt * 32 * 5);
+        w.lx_shift = off;
+        off += round256((size_t)M * 4);
+        w.lx_corr = off;
+        off += round256((size_t)M * w.n_chunks * 8);
+    } else if (kind == PN_BF16 && M >= 1 && M <= 64) {
+        off += round256((size_t)w.n_kb * w.bt * 32 * 11);
+    }
     w.wpitch = off;
     if (repitch) off += round256((size_t)N * w_pitch(KP) * 4);
-    w.acc_cols = (int)(M < 16 ? M : 16);
+    w.acc_cols = (int)(M * cpt < 16 ? M * cpt : 16);
     w.counters = off;
     w.accbuf = off;
     w.zero_bytes = 0;
@@ -1207,7 +1500,7 @@ static WsLayout ws_layout(int kind, int64_t M, int64_t N, int64_t K, bool allow_
         off += round256((size_t)w.n_items * kUnpackWarps * 4);
         w.accbuf = off;
         if (w.bt <= 16) {
-            off += round256((size_t)w.grid * kRows * w.acc_cols * (kind == PN_BF16 ? 8 : 4));
+            off += round256((size_t)w.grid * kRows * w.acc_cols * (kind == PN_BF16 && !l8 ? 8 : 4));
             w.zero_bytes = off - w.counters;  // counters and sums
         } else {
             w.zero_bytes = off - w.counters;  // counters only
@@ -1217,9 +1510,17 @@ static WsLayout ws_layout(int kind, int64_t M, int64_t N, int64_t K, bool allow_
     w.total = off;
     return w;
 }
+static WsLayout ws_layout(int kind, int64_t M, int64_t N, int64_t K, bool allow_split, bool repitch) {
+    return ws_layout_ex(kind, M, N, K, allow_split, repitch, l8_takes(kind, M, K));
+}
 size_t linear_workspace_bytes(int kind, int64_t M, int64_t N, int64_t K, int64_t packed_ld) {
     if (M <= 0 || N <= 0) return 0;
-    const size_t tc = ws_layout(kind, M, N, K, true, packed_ld % 4 != 0).total;
+    size_t tc = ws_layout_ex(kind, M, N, K, true, packed_ld % 4 != 0, false).total;
+    // enough for either tensor-core decode path, whichever pn_set_limb_max_tokens selects
+    if (l8_shape(kind, M, K)) {
+        const size_t t8 = ws_layout_ex(kind, M, N, K, true, packed_ld % 4 != 0, true).total;
+        if (t8 > tc) tc = t8;
+    }
     // bf16 decode batches may run on the CUDA-core GEMV instead (pn_gemv.cu)
     const size_t gv = kind == PN_BF16 ? gemv_workspace_bytes(M, N, (K + kPerWord - 1) / kPerWord) : 0;
     return tc > gv ? tc : gv;
@@ -1341,7 +1642,33 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     prm.xperm = ws + L.xperm;
     // split-tile counters start at zero (the decode pre-pass zeroes them, else a memset)
     const int64_t n_zero16 = L.unit == 1 ? (int64_t)(L.zero_bytes / 16) : 0;
-    if (C::kPerm) {
+    prm.lx_shift = reinterpret_cast<const int*>(ws + L.lx_shift);
+    prm.lx_corr = reinterpret_cast<const long long*>(ws + L.lx_corr);
+    prm.lx_chunks = L.n_chunks;
+    if constexpr (C::kL8) {
+        if (a.M * kL8Cols > BT || a.K > kL8MaxK) {
+            *why = "internal: limb tile too small for the batch";
+            return PN_ERR_ARG;
+        }
+        // chunk blocks per token, plus zeroing-only blocks when the split-tile
+        // sums need them (~4 zeroing stores per thread)
+        int64_t gx = L.n_chunks;
+        const int64_t zx = (n_zero16 / (4 * kLimbThreads) + a.M - 1) / a.M;
+        if (zx > gx) gx = zx < 4096 ? zx : 4096;
+        const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(a.x);
+        uint4* zero = reinterpret_cast<uint4*>(ws + L.counters);
+        // A plain launch, like the bf16 decode pre-pass below; the GEMM is its
+        // programmatic dependent.
+        limb_x_kernel<BT><<<dim3((unsigned)gx, (unsigned)a.M), kLimbThreads, 0, s>>>(
+            xb, (int)a.M, (int)a.K, prm.n_kb, kL8KbPerChunk, L.n_chunks, ws + L.xperm,
+            reinterpret_cast<int*>(ws + L.lx_shift), reinterpret_cast<long long*>(ws + L.lx_corr), zero, n_zero16);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) {
+            *err = e;
+            *why = "limb activation pre-pass launch";
+            return PN_ERR_CUDA;
+        }
+    } else if (C::kPerm) {
         const int64_t total = a.M * (int64_t)prm.n_kb * kKB;
         if (total >= (int64_t)1 << 31) {
             *why = "activation re-layout exceeds 32-bit indexing (K too large)";
@@ -1437,18 +1764,26 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
 
 template <Kind KIND, bool EPI>
 static int launch_kind(const LinearArgs& a, cudaStream_t s, cudaError_t* err, const char** why) {
-    if constexpr (KIND == Kind::F16) {
-        if (a.M <= 8) return launch_bt<KIND, 8, EPI>(a, s, err, why);
-    }
-    if (a.M <= 16) return launch_bt<KIND, 16, EPI>(a, s, err, why);
-    if (a.M <= 32) return launch_bt<KIND, 32, EPI>(a, s, err, why);
-    if (a.M <= 64) return launch_bt<KIND, 64, EPI>(a, s, err, why);
-    if constexpr (KIND == Kind::F16) {
-        // bf16 operands of a 256-token tile leave TMEM room for only 3 operand stages
-        return launch_bt<KIND, 128, EPI>(a, s, err, why);
+    if constexpr (KIND == Kind::L8) {
+        // accumulator columns: four per token
+        if (a.M <= 2) return launch_bt<KIND, 8, EPI>(a, s, err, why);
+        if (a.M <= 4) return launch_bt<KIND, 16, EPI>(a, s, err, why);
+        if (a.M <= 8) return launch_bt<KIND, 32, EPI>(a, s, err, why);
+        return launch_bt<KIND, 64, EPI>(a, s, err, why);
     } else {
-        if (a.M <= 128) return launch_bt<KIND, 128, EPI>(a, s, err, why);
-        return launch_bt<KIND, 256, EPI>(a, s, err, why);
+        if constexpr (KIND == Kind::F16) {
+            if (a.M <= 8) return launch_bt<KIND, 8, EPI>(a, s, err, why);
+        }
+        if (a.M <= 16) return launch_bt<KIND, 16, EPI>(a, s, err, why);
+        if (a.M <= 32) return launch_bt<KIND, 32, EPI>(a, s, err, why);
+        if (a.M <= 64) return launch_bt<KIND, 64, EPI>(a, s, err, why);
+        if constexpr (KIND == Kind::F16) {
+            // bf16 operands of a 256-token tile leave TMEM room for only 3 operand stages
+            return launch_bt<KIND, 128, EPI>(a, s, err, why);
+        } else {
+            if (a.M <= 128) return launch_bt<KIND, 128, EPI>(a, s, err, why);
+            return launch_bt<KIND, 256, EPI>(a, s, err, why);
+        }
     }
 }
 
@@ -1457,6 +1792,8 @@ int launch_linear(const LinearArgs& a, cudaStream_t s, cudaError_t* err, const c
     *why = "";
     if (a.M == 0 || a.N == 0) return PN_OK;
     const bool epi = a.act != kActNone || a.residual != nullptr;
+    if (l8_takes(a.kind, a.M, a.K))
+        return epi ? launch_kind<Kind::L8, true>(a, s, err, why) : launch_kind<Kind::L8, false>(a, s, err, why);
     if (a.kind == PN_BF16)
         return epi ? launch_kind<Kind::F16, true>(a, s, err, why) : launch_kind<Kind::F16, false>(a, s, err, why);
     return epi ? launch_kind<Kind::I8, true>(a, s, err, why) : launch_kind<Kind::I8, false>(a, s, err, why);

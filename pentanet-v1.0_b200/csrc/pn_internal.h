@@ -61,6 +61,11 @@ cudaError_t launch_linear_simt_bf16(const LinearArgs& a, cudaStream_t s);
 
 int device_sm_count();
 
+// Limb decode (bf16 products of at most l8_max_tokens() tokens, 0..16) on the
+// kind::i8 tensor cores; set_l8_max_tokens clamps to that range.
+int l8_max_tokens();
+void set_l8_max_tokens(int m);
+
 // CUDA-core decode GEMV (pn_gemv.cu) for bf16 products of at most
 // gemv_max_tokens() tokens (settable up to kGemvMaxTokens) whose packed rows
 // sit at a 16-byte pitch; its workspace is gemv_workspace_bytes(M, N, KP).
