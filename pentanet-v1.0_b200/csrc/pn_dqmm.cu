@@ -1189,11 +1189,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Positions past K are zero; rows >= M are not written (their accumulator
 // columns are never read back).
 //
-// One block per (token, k-block) at a time, one thread per position of the
-// k-block (160 threads, five warps): every thread loads, scales and stores one
-// value, and the k-block's sum is a fixed-order reduction (a shuffle tree per
-// warp, then the five warp sums in order), so the result is deterministic.
+// One block per (group of kPermTok tokens, k-block) at a time, one thread per
+// position of the k-block (160 threads, five warps): every thread loads,
+// scales and stores the value of each of the group's tokens (independent
+// loads in flight together), and each token's k-block sum is a fixed-order
+// reduction (a shuffle tree per warp, then the five warp sums in order), so
+// the result is deterministic.
 constexpr int kPermThreads = kKB;
+constexpr int kPermTok = 4;
 template <int BT>
 __global__ void __launch_bounds__(kPermThreads) permute_x_kernel(const __nv_bfloat16* __restrict__ x, int M, int64_t K,
                                                         int n_kb, uint8_t* __restrict__ out, uint4* __restrict__ zero,
@@ -1206,7 +1209,7 @@ __global__ void __launch_bounds__(kPermThreads) permute_x_kernel(const __nv_bflo
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_zero16; i += (int64_t)gridDim.x * blockDim.x)
         zero[i] = make_uint4(0, 0, 0, 0);
     constexpr int kStage = BT * 32 * 11;
-    __shared__ float warp_sum[kPermThreads / 32];
+    __shared__ float warp_sum[kPermTok][kPermThreads / 32];
     const uint32_t e = threadIdx.x;  // position in the k-block
     const uint32_t grp = e / kPerWord;
     const int q = (int)(e - grp * kPerWord);
@@ -1215,28 +1218,43 @@ __global__ void __launch_bounds__(kPermThreads) permute_x_kernel(const __nv_bflo
     // * 2^(133 - 67 - perm_exp(q)), exact
     const float vscale = __int_as_float((127 + 133 - kPermUnitExp - perm_exp(q)) << 23);
     // 32-bit index arithmetic (the host checks M * n_kb * 160 < 2^31)
-    const uint32_t pairs = (uint32_t)M * (uint32_t)n_kb;
+    const uint32_t groups = ((uint32_t)M + kPermTok - 1) / kPermTok;
+    const uint32_t pairs = groups * (uint32_t)n_kb;
     for (uint32_t mk = blockIdx.x; mk < pairs; mk += gridDim.x) {
-        const uint32_t m = mk / (uint32_t)n_kb;
-        const uint32_t kb = mk - m * (uint32_t)n_kb;
-        uint8_t* const kbase = out + (size_t)kb * kStage + m * 32;
-        const uint32_t flip = (m >> 2) & 1;  // 32-byte swizzle: 16-byte halves swap every 4 rows
+        const uint32_t mg = mk / (uint32_t)n_kb;
+        const uint32_t kb = mk - mg * (uint32_t)n_kb;
         const uint32_t ksrc = kb * kKB + src;
-        const float v = ksrc < (uint64_t)K ? __bfloat162float(x[(size_t)m * K + ksrc]) : 0.0f;
-        *reinterpret_cast<__nv_bfloat16*>(kbase + j * (BT * 32) + (((ee >> 3) ^ flip) << 4) + (ee & 7) * 2) =
-            __float2bfloat16_rn(__fmul_rn(v, vscale));
-        float sum = v;
-        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 16));
-        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 8));
-        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 4));
-        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 2));
-        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 1));
-        if ((e & 31) == 0) warp_sum[e >> 5] = sum;
-        __syncthreads();
-        if (e == 0) {
-            float t = warp_sum[0];
+        float v[kPermTok];
 #pragma unroll
-            for (int w = 1; w < kPermThreads / 32; ++w) t = __fadd_rn(t, warp_sum[w]);
+        for (int t = 0; t < kPermTok; ++t) {
+            const uint32_t m = mg * kPermTok + t;
+            v[t] = (m < (uint32_t)M && ksrc < (uint64_t)K) ? __bfloat162float(x[(size_t)m * K + ksrc]) : 0.0f;
+        }
+#pragma unroll
+        for (int t = 0; t < kPermTok; ++t) {
+            const uint32_t m = mg * kPermTok + t;
+            if (m < (uint32_t)M) {
+                uint8_t* const kbase = out + (size_t)kb * kStage + m * 32;
+                const uint32_t flip = (m >> 2) & 1;  // 32-byte swizzle: 16-byte halves swap every 4 rows
+                *reinterpret_cast<__nv_bfloat16*>(kbase + j * (BT * 32) + (((ee >> 3) ^ flip) << 4) + (ee & 7) * 2) =
+                    __float2bfloat16_rn(__fmul_rn(v[t], vscale));
+            }
+            float sum = v[t];
+            sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 16));
+            sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 8));
+            sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 4));
+            sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 2));
+            sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 1));
+            if ((e & 31) == 0) warp_sum[t][e >> 5] = sum;
+        }
+        __syncthreads();
+        if (e < kPermTok && mg * kPermTok + e < (uint32_t)M) {
+            const uint32_t m = mg * kPermTok + e;
+            uint8_t* const kbase = out + (size_t)kb * kStage + m * 32;
+            const uint32_t flip = (m >> 2) & 1;
+            float t = warp_sum[e][0];
+#pragma unroll
+            for (int w = 1; w < kPermThreads / 32; ++w) t = __fadd_rn(t, warp_sum[e][w]);
             t = __fmul_rn(t, -0x1p-66f);  // -2 * 2^-67 * sum, exact
             const __nv_bfloat16 p1 = __float2bfloat16_rn(t);
             const float r1 = __fsub_rn(t, __bfloat162float(p1));
@@ -1674,8 +1692,8 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
             *why = "activation re-layout exceeds 32-bit indexing (K too large)";
             return PN_ERR_UNSUPPORTED;
         }
-        // one block per (token, k-block); extra blocks when the zeroing needs them
-        int64_t want = a.M * (int64_t)prm.n_kb;
+        // one block per (token group, k-block); extra blocks when the zeroing needs them
+        int64_t want = ((a.M + kPermTok - 1) / kPermTok) * (int64_t)prm.n_kb;
         if (n_zero16 / (4 * kPermThreads) > want) want = n_zero16 / (4 * kPermThreads);  // ~4 zeroing stores per thread
         const int blocks = (int)(want < 4096 ? (want > 0 ? want : 1) : 4096);
         const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(a.x);
