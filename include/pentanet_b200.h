@@ -92,6 +92,17 @@ int pn_quantize_pack_ternary(const void *w, int w_dtype, int64_t N, int64_t K, c
 /* out[n, k] = ((packed[n, k/10] >> 3*(k%10)) & 7) - 2 as int8, k < K_orig. */
 int pn_unpack(const int32_t *packed, int64_t N, int64_t K_packs, int64_t K_orig, int8_t *out, void *stream);
 
+/* The reference's CPU matmul on the GPU: out (M, N) fp32 = scale * x . w^T
+ * for fp32 x (M, K) and unpacked int8 weights w (N, K) in {-2..+2} (from
+ * pn_unpack), both row-major contiguous; replaces penta_matmul_avx2
+ * (penta_avx2.c:87-95, bound by penta_avx2_wrapper.py:27-34) with the same
+ * argument order plus a stream and a status.  fp32 sums of exact products,
+ * multiplied by scale once; within fp32 rounding of the reference's result
+ * (the summation order differs).  Reads 8 bits per weight: the packed
+ * entry points below are the fast path. */
+int pn_matmul_i8w(const float *x, const int8_t *w, float *out, int64_t M, int64_t N, int64_t K, float scale,
+                  void *stream);
+
 /* ---- fused dequant-matmul: replaces penta_linear / _penta_matmul_kernel
  *      (penta_kernel.py:111-278) ------------------------------------------- */
 

@@ -14,3 +14,4 @@
 #include "pn_capi.cu"
 #include "pn_static_ws.cu"
 #include "pn_peer.cu"
+#include "pn_i8w.cu"

@@ -124,6 +124,30 @@ def unpack_weights_i8(packed: torch.Tensor, K_orig: int) -> torch.Tensor:
     return out
 
 
+def penta_linear_i8w(x: torch.Tensor, w_int8: torch.Tensor, scale: float,
+                     bias: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 x (..., K) times unpacked int8 weights (N, K) in {-2..+2}, times
+    scale, plus an optional bias, in fp32: the GPU form of the reference's
+    AVX2 path (penta_linear_avx2, penta_avx2_wrapper.py:58-94, computing
+    penta_matmul_avx2, penta_avx2.c:87-171).  w_int8 comes from
+    unpack_weights_i8 (the layout of penta_unpack_3bit)."""
+    assert w_int8.dim() == 2 and w_int8.dtype == torch.int8, "w_int8 must be an (N, K) int8 tensor"
+    _require_cuda(x, "penta_linear_i8w")
+    _require_cuda(w_int8, "penta_linear_i8w")
+    N, K = w_int8.shape
+    assert x.shape[-1] == K, f"x has K={x.shape[-1]}, the weights K={K}"
+    lead = x.shape[:-1]
+    xf = x.reshape(-1, K).float().contiguous()
+    w = w_int8.contiguous()
+    M = xf.shape[0]
+    y = torch.empty(M, N, dtype=torch.float32, device=x.device)
+    _nat.check(_nat.load().pn_matmul_i8w(xf.data_ptr(), w.data_ptr(), y.data_ptr(), M, N, K, float(scale),
+                                         _nat.stream_of(xf)), "penta_linear_i8w")
+    if bias is not None:
+        y = y + bias.float()
+    return y.reshape(*lead, N)
+
+
 def memory_stats(N: int, K: int) -> dict:
     """Memory footprint comparison for an (N, K) weight matrix (penta_kernel.py:93-106):
     nominal 3 bits/weight, as the reference reports it."""

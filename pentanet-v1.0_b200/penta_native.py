@@ -31,7 +31,7 @@ EXPORTS = (
     "pn_linear_i8_ld", "pn_linear_i8_epi", "pn_layer_norm",
     "pn_ipc_handle", "pn_ipc_open", "pn_ipc_close",
     "pn_linear_bf16_peers", "pn_peer_barrier", "pn_peer_barrier_wait", "pn_set_gemv_max_tokens",
-    "pn_set_limb_max_tokens",
+    "pn_set_limb_max_tokens", "pn_matmul_i8w",
 )
 
 _lib = None
@@ -88,6 +88,7 @@ def load() -> ctypes.CDLL:
         "pn_peer_barrier_wait": (I, [ctypes.POINTER(P), I, I, P, I64, P]),
         "pn_set_gemv_max_tokens": (I, [I]),
         "pn_set_limb_max_tokens": (I, [I]),
+        "pn_matmul_i8w": (I, [P, P, P, I64, I64, I64, F, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
