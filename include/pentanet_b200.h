@@ -92,6 +92,22 @@ int pn_quantize_pack_ternary(const void *w, int w_dtype, int64_t N, int64_t K, c
 /* out[n, k] = ((packed[n, k/10] >> 3*(k%10)) & 7) - 2 as int8, k < K_orig. */
 int pn_unpack(const int32_t *packed, int64_t N, int64_t K_packs, int64_t K_orig, int8_t *out, void *stream);
 
+/* ---- ternary weights in 2 bits (no counterpart in the reference's packed
+ *      format; the rule is QuantLinear's bitnet mode, train_pentagpt.py:33-36).
+ * Sixteen codes per int32, code = q + 1 in {0, 1, 2} at bits 2j..2j+1 for
+ * k = 16g + j of word g, rows of pn_words_2bit(K) = ceil(K/16) words,
+ * padding code 1 (q = 0); q = clamp(round_half_even(w / gamma), -1, 1) with
+ * gamma from pn_absmean_scale (device pointer), rounded as pn_quantize_pack.
+ * pn_linear_bf16_2bit: y = x . q^T * scale (+ bias) with fp32 sums and the
+ * output rounding of pn_linear_bf16, on CUDA cores (a format path: 2 bits
+ * per weight read, not tuned); a code 3 reads as q = 2. */
+int64_t pn_words_2bit(int64_t K);
+int pn_quantize_pack_2bit(const void *w, int w_dtype, int64_t N, int64_t K, const float *d_scale, int32_t *packed,
+                          void *stream);
+int pn_unpack_2bit(const int32_t *packed, int64_t N, int64_t K_words, int64_t K_orig, int8_t *out, void *stream);
+int pn_linear_bf16_2bit(const void *x, int64_t M, int64_t K, const int32_t *packed, int64_t N, int64_t K_words,
+                        float scale, const void *bias, void *y, int y_dtype, void *stream);
+
 /* The reference's CPU matmul on the GPU: out (M, N) fp32 = scale * x . w^T
  * for fp32 x (M, K) and unpacked int8 weights w (N, K) in {-2..+2} (from
  * pn_unpack), both row-major contiguous; replaces penta_matmul_avx2

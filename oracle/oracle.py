@@ -116,6 +116,29 @@ def unpack_np(packed: np.ndarray, K: int) -> np.ndarray:
     return (codes.reshape(N, KP * PER_WORD)[:, :K].astype(np.int16) - 2).astype(np.int8)
 
 
+def pack_2bit(q: np.ndarray) -> np.ndarray:
+    """Ternary values q (N, K) in {-1, 0, +1} in the library's 2-bit format:
+    sixteen codes q + 1 per int32, k = 16g + j at bits 2j..2j+1 of word g,
+    padding code 1.  The ternary rule itself is QuantLinear's bitnet mode
+    (train_pentagpt.py:33-36), which quantize_pack(..., mode='bitnet')
+    restates; the reference has no 2-bit packed format."""
+    q = np.asarray(q, dtype=np.int64)
+    N, K = q.shape
+    KW = (K + 15) // 16
+    codes = np.ones((N, KW * 16), dtype=np.uint64)
+    codes[:, :K] = q + 1
+    words = (codes.reshape(N, KW, 16) << (2 * np.arange(16, dtype=np.uint64))[None, None, :]).sum(axis=2)
+    return words.astype(np.uint32).view(np.int32)
+
+
+def unpack_2bit(packed: np.ndarray, K: int) -> np.ndarray:
+    """pack_2bit's inverse -> int8 (N, K); a code 3 reads as 2."""
+    p = np.ascontiguousarray(packed).view(np.uint32)
+    N, KW = p.shape
+    codes = (p[:, :, None] >> (2 * np.arange(16, dtype=np.uint32))[None, None, :]) & np.uint32(3)
+    return (codes.reshape(N, KW * 16)[:, :K].astype(np.int16) - 1).astype(np.int8)
+
+
 # ----------------------------------------------------------------- matmul ---
 
 def matmul_f32(x: np.ndarray, w8: np.ndarray, gamma: float) -> np.ndarray:

@@ -18,7 +18,7 @@ ROOT = os.path.dirname(HERE)
 OUT = os.path.join(HERE, "libpentanet_b200.so")
 SOURCES = ["csrc/pn_lib.cu"]
 DEPS = ["csrc/pn_common.cuh", "csrc/pn_internal.h", "csrc/pn_pack.cu", "csrc/pn_act.cu", "csrc/pn_norm.cu",
-        "csrc/pn_dqmm.cu", "csrc/pn_simt.cu", "csrc/pn_gemv.cu", "csrc/pn_capi.cu", "csrc/pn_static_ws.cu", "csrc/pn_peer.cu", "csrc/pn_i8w.cu",
+        "csrc/pn_dqmm.cu", "csrc/pn_simt.cu", "csrc/pn_gemv.cu", "csrc/pn_capi.cu", "csrc/pn_static_ws.cu", "csrc/pn_peer.cu", "csrc/pn_i8w.cu", "csrc/pn_ternary2.cu",
         "csrc/pn_lib.cu", "../include/pentanet_b200.h"]
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",

@@ -15,3 +15,4 @@
 #include "pn_static_ws.cu"
 #include "pn_peer.cu"
 #include "pn_i8w.cu"
+#include "pn_ternary2.cu"

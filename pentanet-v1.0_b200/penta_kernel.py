@@ -106,6 +106,67 @@ def quantize_and_pack(weight: torch.Tensor, scale: float | torch.Tensor | None =
     return packed, K, float(d_scale)
 
 
+def quantize_and_pack_2bit(weight: torch.Tensor, scale: float | torch.Tensor | None = None
+                           ) -> tuple[torch.Tensor, int, float]:
+    """The ternary rule of QuantLinear(mode='bitnet') (train_pentagpt.py:33-36)
+    packed 16 weights per int32 (2 bits each, code q + 1): 37.5 % fewer bytes
+    than the 3-bit format.  Returns (packed (N, ceil(K/16)) int32, K, scale).
+    Not in the reference."""
+    assert weight.dim() == 2
+    _require_cuda(weight, "quantize_and_pack_2bit")
+    N, K = weight.shape
+    w = weight.detach().contiguous()
+    if w.dtype not in (torch.float32, torch.bfloat16):
+        w = w.float()
+    if scale is None:
+        d_scale = absmean_scale(w)
+    elif isinstance(scale, torch.Tensor):
+        d_scale = scale.detach().to(device=w.device, dtype=torch.float32).reshape(())
+    else:
+        d_scale = torch.tensor(float(scale), dtype=torch.float32, device=w.device)
+    L = _nat.load()
+    packed = torch.empty(N, int(L.pn_words_2bit(K)), dtype=torch.int32, device=w.device)
+    dt = _nat.PN_F32 if w.dtype == torch.float32 else _nat.PN_BF16
+    _nat.check(L.pn_quantize_pack_2bit(w.data_ptr(), dt, N, K, d_scale.data_ptr(), packed.data_ptr(),
+                                       _nat.stream_of(w)), "quantize_and_pack_2bit")
+    return packed, K, float(d_scale)
+
+
+def unpack_weights_2bit(packed: torch.Tensor, K_orig: int) -> torch.Tensor:
+    """The 2-bit ternary format back to int8 (N, K_orig) values in {-1, 0, +1}."""
+    assert packed.dim() == 2 and packed.dtype == torch.int32
+    _require_cuda(packed, "unpack_weights_2bit")
+    N, KW = packed.shape
+    p = packed.contiguous()
+    out = torch.empty(N, K_orig, dtype=torch.int8, device=p.device)
+    _nat.check(_nat.load().pn_unpack_2bit(p.data_ptr(), N, KW, K_orig, out.data_ptr(), _nat.stream_of(p)),
+               "unpack_weights_2bit")
+    return out
+
+
+def penta_linear_2bit(x: torch.Tensor, packed_w: torch.Tensor, scale: float, K_orig: int,
+                      bias: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """penta_linear for weights in the 2-bit ternary format: bf16 x (..., K),
+    fp32 sums, then scale, bias and the output rounding of penta_linear."""
+    assert x.dtype == torch.bfloat16, "x must be bfloat16"
+    assert packed_w.dim() == 2 and packed_w.dtype == torch.int32
+    assert x.shape[-1] == K_orig, f"x has K={x.shape[-1]}, expected {K_orig}"
+    assert out_dtype in (torch.bfloat16, torch.float32)
+    _require_cuda(x, "penta_linear_2bit")
+    N, KW = packed_w.shape
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, K_orig).contiguous()
+    M = x2.shape[0]
+    w = packed_w.contiguous()
+    b = None if bias is None else bias.to(device=x.device, dtype=torch.bfloat16).contiguous()
+    y = torch.empty(M, N, dtype=out_dtype, device=x.device)
+    _nat.check(_nat.load().pn_linear_bf16_2bit(x2.data_ptr(), M, K_orig, w.data_ptr(), N, KW, float(scale),
+                                               None if b is None else b.data_ptr(), y.data_ptr(),
+                                               _nat.PN_F32 if out_dtype == torch.float32 else _nat.PN_BF16,
+                                               _nat.stream_of(x2)), "penta_linear_2bit")
+    return y.reshape(*lead, N)
+
+
 def unpack_weights(packed: torch.Tensor, K_orig: int) -> torch.Tensor:
     """Unpack 3-bit tensor -> int32 (N, K_orig) with values in {-2..+2}
     (penta_kernel.py:81-90).  Use unpack_weights_i8 for the int8 form."""

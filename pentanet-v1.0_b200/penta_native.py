@@ -32,6 +32,7 @@ EXPORTS = (
     "pn_ipc_handle", "pn_ipc_open", "pn_ipc_close",
     "pn_linear_bf16_peers", "pn_peer_barrier", "pn_peer_barrier_wait", "pn_set_gemv_max_tokens",
     "pn_set_limb_max_tokens", "pn_matmul_i8w",
+    "pn_words_2bit", "pn_quantize_pack_2bit", "pn_unpack_2bit", "pn_linear_bf16_2bit",
 )
 
 _lib = None
@@ -89,6 +90,10 @@ def load() -> ctypes.CDLL:
         "pn_set_gemv_max_tokens": (I, [I]),
         "pn_set_limb_max_tokens": (I, [I]),
         "pn_matmul_i8w": (I, [P, P, P, I64, I64, I64, F, P]),
+        "pn_words_2bit": (I64, [I64]),
+        "pn_quantize_pack_2bit": (I, [P, I, I64, I64, P, P, P]),
+        "pn_unpack_2bit": (I, [P, I64, I64, I64, P, P]),
+        "pn_linear_bf16_2bit": (I, [P, I64, I64, P, I64, I64, F, P, P, I, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
