@@ -53,8 +53,11 @@ def test_ties_and_roundtrip(cuda_device):
         assert torch.equal(pk.unpack_weights(packed, K).cpu(), w_true)
 
 
-@pytest.mark.parametrize("N,K", [(1, 1), (3, 9), (2, 11), (129, 1001), (300, 4096), (7, 28672)])
+@pytest.mark.parametrize("N,K", [(1, 1), (3, 9), (2, 11), (129, 1001), (300, 4096), (7, 28672),
+                                 (3, 4), (5, 124), (17, 8200), (9, 8192)])
 def test_pack_random_shapes_vs_oracle(cuda_device, N, K):
+    """Ragged and aligned K, odd word counts, a partial last word: the
+    oracle's bytes."""
     w = gen_weight(N, K, seed=N * 31 + K, std=0.3)
     want, _, gamma = orc.quantize_pack(w.numpy())
     got, _, g2 = pk.quantize_and_pack(w.to(cuda_device))
