@@ -32,6 +32,9 @@ __global__ void __launch_bounds__(kActThreads) quant_act_i8_kernel(const T* __re
                                                                    int8_t* __restrict__ xq, int64_t pitch,
                                                                    float* __restrict__ s_x,
                                                                    int32_t* __restrict__ rowsum) {
+    // The product that reads this output may start its prologue and weight
+    // streaming now (it waits for this grid before reading the output).
+    asm volatile("griddepcontrol.launch_dependents;");
     __shared__ float red_f[kActThreads / 32];
     __shared__ int red_i[kActThreads / 32];
     const int64_t m = blockIdx.x;
@@ -107,6 +110,9 @@ __global__ void __launch_bounds__(kActThreads) quant_act_i8_vec_kernel(const uin
                                                                        int64_t K, int8_t* __restrict__ xq,
                                                                        int64_t pitch, float* __restrict__ s_x,
                                                                        int32_t* __restrict__ rowsum) {
+    // The product that reads this output may start its prologue and weight
+    // streaming now (it waits for this grid before reading the output).
+    asm volatile("griddepcontrol.launch_dependents;");
     constexpr int kTokens = kActThreads / TPT;  // tokens per block
     constexpr int kWarpsPerToken = TPT / 32;     // 0 when a warp holds several tokens
     constexpr int kShfl = TPT < 32 ? TPT : 32;   // lanes of one token inside a warp

@@ -545,8 +545,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // soon as its own MMAs release them: a slow issuer never holds back
         // the copies of the others.
         if (lane == 0) {
-            // (decode tiles read the pre-pass's output: wait for that grid)
-            if (C::kPerm) asm volatile("griddepcontrol.wait;" ::: "memory");
+            // The activations are the previous grid's output (the decode
+            // pre-pass, the int8 quantiser or whatever produced x): every
+            // GEMM is a programmatic dependent, so wait for that grid.
+            asm volatile("griddepcontrol.wait;" ::: "memory");
             const int64_t u_begin = range_begin(p, blockIdx.x);
             uint32_t total = (uint32_t)(2 * (range_begin(p, blockIdx.x + 1) - u_begin));
             if (C::kXByWLoader && total > (uint32_t)C::kActEarly) total = C::kActEarly;  // the rest: weight loaders
@@ -840,8 +842,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
 
             // ------------------------------------------------- epilogue ----
-            // Split-tile counters are zeroed by the decode pre-pass: wait for that grid.
-            if (C::kPerm) asm volatile("griddepcontrol.wait;" ::: "memory");
+            // The epilogue reads what the previous grid wrote (split-tile
+            // counters zeroed by the decode pre-pass, per-token scales and row
+            // sums of the quantiser, a residual) and writes outputs it may
+            // still read: wait for that grid.
+            asm volatile("griddepcontrol.wait;" ::: "memory");
             // Issuer (it_item + a) % kIssuers accumulated k-blocks of this segment
             // iff a < its k-block count (segments are at least 2 k-blocks long).
             if (!warp_wait(acc_full, n_local & 1, abort_flag)) { ok = false; break; }
@@ -1753,10 +1758,13 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
     }
     const int grid = L.grid;
     cudaError_t e;
-    if (C::kPerm) {
+    {
         // Programmatic dependent launch: the GEMM's prologue, TMEM allocation
-        // and weight streaming overlap the activation pre-pass; the threads
-        // that read its results wait for it (griddepcontrol.wait).
+        // and weight streaming overlap the grid before it (the decode
+        // pre-pass, the int8 quantiser, a LayerNorm: kernels that let their
+        // dependents start early); the threads that read that grid's results
+        // wait for it (griddepcontrol.wait).  After a kernel that does not
+        // trigger early it simply starts when that kernel ends.
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(grid);
         cfg.blockDim = dim3(kThreads);
@@ -1768,9 +1776,6 @@ static int launch_bt(const LinearArgs& a, cudaStream_t s, cudaError_t* err, cons
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         e = cudaLaunchKernelEx(&cfg, kern, xmap, xmap_tail, wmap, prm);
-    } else {
-        kern<<<grid, kThreads, C::kSmem, s>>>(xmap, xmap_tail, wmap, prm);
-        e = cudaGetLastError();
     }
     if (e != cudaSuccess) {
         *err = e;

@@ -76,6 +76,9 @@ __global__ void __launch_bounds__(kNormWarps * 32, 5) layer_norm_reg_kernel(cons
                                                                          const float* __restrict__ w,
                                                                          const float* __restrict__ b, float eps,
                                                                          void* __restrict__ y, int y_f32) {
+    // The product that reads this output may start its prologue and weight
+    // streaming now (it waits for this grid before reading the output).
+    asm volatile("griddepcontrol.launch_dependents;");
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * kNormWarps + (threadIdx.x >> 5);
     if (row >= M) return;
@@ -156,6 +159,9 @@ __global__ void __launch_bounds__(kNormWarps * 32) layer_norm_any_kernel(const T
                                                                          const float* __restrict__ w,
                                                                          const float* __restrict__ b, float eps,
                                                                          void* __restrict__ y, int y_f32) {
+    // The product that reads this output may start its prologue and weight
+    // streaming now (it waits for this grid before reading the output).
+    asm volatile("griddepcontrol.launch_dependents;");
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * kNormWarps + (threadIdx.x >> 5);
     if (row >= M) return;
