@@ -590,6 +590,27 @@ def pack_secondary(dev, peaks):
     return res
 
 
+def gpt_roofline(gpt: dict, peaks: dict, world: int) -> dict:
+    """Tensor roofline of the bf16 PentaGPT-124M forward.  Algorithmic FLOPs
+    per forward of B x T tokens: the four projections of each of the 12
+    layers, 2 (3 + 1 + 4 + 4) d^2 per token (d = 768); causal attention,
+    QK^T and AV over the T/2 earlier positions on average, 2 T d per token
+    per layer; the tied lm_head on the last position of each sequence,
+    2 d V (V = 50257)."""
+    B, T, d, L, V = 32, 1024, 768, 12, 50257
+    proj = 2.0 * (3 + 1 + 4 + 4) * d * d * L * B * T
+    attn = 2.0 * T * d * L * B * T
+    head = 2.0 * d * V * B
+    flops = proj + attn + head
+    achieved = flops / (gpt["bf16"]["ms_per_forward"] * 1e-3) / 1e12
+    peak = peaks["bf16_tflops"] * world
+    return {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4), "flops_per_forward": flops,
+            "peak_source": "measured dense bf16 (MEASURED_PEAKS.json) per GPU x GPUs"
+                           if peaks.get("source") != "fallback" else "fallback",
+            "note": "projections run as packed-weight bf16 products, attention as torch SDPA"}
+
+
 def pentagpt_forward(dev, world: int = 1, rank: int = 0):
     """Secondary measurement: PentaGPT-124M forward (prefill) tokens/s -- 12
     layers, d 768, every projection packed, batch 32 x 1024 random token ids,
@@ -963,6 +984,7 @@ def run_ours(args):
     if not args.no_prefill:
         prefill = prefill_int8(dev, gen, peaks, world, rank)
         gpt = pentagpt_forward(dev, world, rank)
+        gpt["roofline"] = gpt_roofline(gpt, peaks, world)
         if world == 1:
             packsec = pack_secondary(dev, peaks)
     if prefill is not None and prefill.get("parity", "bit-exact") != "bit-exact":
